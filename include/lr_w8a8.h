@@ -1,0 +1,154 @@
+/*
+ * lr_w8a8.h — C ABI of the B200 (sm_100a) W8A8 projection path of
+ * LynnReal-Omni Flash DiT blocks.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a cudaStream_t passed as void*;
+ *   - launches asynchronously on that stream and never synchronises;
+ *   - allocates nothing: outputs are caller-owned buffers;
+ *   - returns LR_OK or an error status; lr_last_error() then holds a message.
+ *
+ * Tensor conventions (all row-major, C-contiguous unless a stride is given):
+ *   bf16 values are passed as `const void*` / `void*` (2 bytes per element);
+ *   `indices` are int64 adaLN table rows, one per token of the sequence: the
+ *   table row of flattened row r is indices[r % sequence]
+ *   (model/kernels.py:62-63,98-99,144-145);
+ *   `table` is the bf16 adaLN modulation table [table_rows, table_width] with
+ *   slot s occupying columns [s*hidden, (s+1)*hidden) (model/fusion.py:69).
+ *
+ * Numerics follow model/kernels.py and model/int8_gemm.py with IEEE
+ * division / square root and no FMA contraction; the rounding points are
+ * documented per function.
+ */
+#ifndef LR_W8A8_H
+#define LR_W8A8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define LR_OK 0
+#define LR_ERR_INVALID_ARGUMENT 1 /* contract violation (reference raises ValueError) */
+#define LR_ERR_UNSUPPORTED 2      /* shape or alignment this build does not handle */
+#define LR_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
+
+/* GEMM epilogues (lr_int8_gemm). */
+#define LR_EPI_NONE 0          /* bf16((acc*rs)*cs + bias) */
+#define LR_EPI_GELU_TANH 1     /* bf16(gelu_tanh(bf16((acc*rs)*cs + bias))) */
+#define LR_EPI_GATED_RESIDUAL 2 /* bf16(x + bf16(gate * bf16((acc*rs)*cs + bias))) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lr_version(void);
+
+/* Message describing the last error returned on this host thread ("" if none). */
+const char* lr_last_error(void);
+
+/* Read (and, if clear != 0, reset) the device status bits of the current device.
+ * Bit 0: an adaLN index was outside [0, table_rows) (that row used a zero
+ * modulation); bit 1: a bounded wait inside the GEMM gave up. Synchronises the
+ * device. */
+int lr_device_status(unsigned int* bits, int clear);
+
+/* K1 — per-row dynamic int8 quantisation.
+ * Replaces model/kernels.py:19-24 `quantize_rows` (kernel :8-16) and the torch
+ * quantiser of Int8Linear.forward, model/int8.py:66-67.
+ *   scale[r] = max(max_j |x[r,j]|, 1e-8) / 127        (fp32)
+ *   q[r,j]   = round_half_even(clamp(x[r,j] / scale[r], -127, 127))
+ * x: bf16 [rows, width] with row stride `row_stride` elements (>= width);
+ * q: int8 [rows, width] contiguous; scales: fp32 [rows]. */
+int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
+                     int8_t* q, float* scales, void* stream);
+
+/* K2 — standalone int32 -> bf16 dequant epilogue.
+ * Replaces model/kernels.py:41-46 `int8_epilogue` (kernel :27-38), used by
+ * Int8Linear.forward_quantized with gemm="torch" and fused_ops (model/int8.py:52-54).
+ *   out[m,n] = bf16((float(acc[m,n]) * row_scale[m]) * col_scale[n] + bias[n])
+ * bias may be NULL. */
+int lr_int8_epilogue(const int32_t* acc, int64_t rows, int64_t cols, const float* row_scale,
+                     const float* col_scale, const void* bias, void* out, void* stream);
+
+/* K3 — RMSNorm + adaLN modulate, bf16 output.
+ * Replaces model/kernels.py:260-272 `_rms_adaln` (kernel :48-78).
+ *   r   = 1 / sqrt(sum_j x^2 / hidden + eps)
+ *   n   = bf16((x * r) * w)
+ *   out = bf16(bf16(n * bf16(1 + table[.., scale_slot])) + table[.., shift_slot])
+ * x, out: bf16 [rows, hidden]; norm_weight: bf16 [hidden]. */
+int lr_rms_adaln(const void* x, const void* norm_weight, float eps, const void* table,
+                 int64_t table_rows, int64_t table_width, const int64_t* indices, int64_t sequence,
+                 int64_t rows, int64_t hidden, int shift_slot, int scale_slot, void* out,
+                 void* stream);
+
+/* K4 (+K8) — RMSNorm + adaLN modulate + per-row int8 quantisation.
+ * Replaces model/kernels.py:275-289 `_rms_adaln_quant_int8` (kernel :81-128)
+ * and, when `update` is non-NULL, model/kernels.py:405-419 `residual_rms_quant`
+ * (the kernel's WITH_RESIDUAL branch, :101-105):
+ *   v = x;  if update: v = bf16(x + bf16(table[.., gate_slot] * update)),
+ *                      residual_out = v
+ *   m = bf16(bf16(n * bf16(1 + scale)) + shift) with n as in lr_rms_adaln
+ *   scales[r] = max(max_j |m|, 1e-8) / 127; q = RNE(clamp(m / scales[r], +-127))
+ * table may be NULL: then no modulation is applied (m = n) and the gate is 1
+ * (a plain RMSNorm + quantiser, used for slot-free prologues). */
+int lr_rms_adaln_quant_int8(const void* x, const void* norm_weight, float eps, const void* table,
+                            int64_t table_rows, int64_t table_width, const int64_t* indices,
+                            int64_t sequence, int64_t rows, int64_t hidden, int shift_slot,
+                            int scale_slot, const void* update, int gate_slot, void* residual_out,
+                            int8_t* q, float* scales, void* stream);
+
+/* K5 — gated residual.
+ * Replaces model/kernels.py:292-304 `_gated_residual` (kernel :131-153):
+ *   out = bf16(x + bf16(table[indices[r % sequence], gate_slot*hidden + j] * y))
+ * table may be NULL (gate = 1: a plain bf16 residual add). */
+int lr_gated_residual(const void* x, const void* y, const void* table, int64_t table_rows,
+                      int64_t table_width, const int64_t* indices, int64_t sequence, int64_t rows,
+                      int64_t hidden, int gate_slot, void* out, void* stream);
+
+/* K6 — SwiGLU on a [rows, 2*inner] projection (value | gate halves).
+ * Replaces model/kernels.py:307-315 `_swiglu` (kernel :156-166):
+ *   out = bf16(value * bf16(gate * sigmoid(gate))) */
+int lr_swiglu(const void* projected, int64_t rows, int64_t inner, void* out, void* stream);
+
+/* K7 — SwiGLU + per-row int8 quantisation.
+ * Replaces model/kernels.py:318-328 `_swiglu_quant_int8` (kernel :169-185). */
+int lr_swiglu_quant_int8(const void* projected, int64_t rows, int64_t inner, int8_t* q,
+                         float* scales, void* stream);
+
+/* K10 (+K2 fused) — INT8 GEMM with int32 accumulation and a fused bf16 epilogue.
+ * Replaces model/int8_gemm.py:200-267 `int8_matmul` (kernel `_gemm` :117-150),
+ * model/int8_tma.py:299-308 `matmul`, and the GEMM inside
+ * Int8Linear.forward_quantized (model/int8.py:41-58).
+ *   acc[m,n] = sum_k a[m,k] * b[k,n]                       (exact int32)
+ *   d[m,n]   = (float(acc) * row_scale[m]) * col_scale[n] (+ bias[n])
+ * a: int8 [M, K], row stride lda (elements, >= K);
+ * b: int8 weights addressed as b[k*b_stride_k + n*b_stride_n] — the
+ *    reference's `weight_int8` is the [K, N] transpose view of a row-major
+ *    [N, K] matrix, i.e. b_stride_k = 1, b_stride_n = K (model/int8.py:12,33);
+ * row_scale: fp32 [M]; col_scale: fp32 [N]; bias: bf16 [N] or NULL;
+ * out: bf16 [M, N] row stride ldo.
+ * epilogue LR_EPI_GATED_RESIDUAL additionally reads the residual stream
+ * `resid` (bf16 [M, N], row stride ldr; may alias `out` only if ldr == ldo)
+ * and the gate table[indices[m % sequence], gate_slot*N + n]; `table` may be
+ * NULL for gate = 1 (plain residual add). Unused residual arguments may be 0/NULL.
+ * The tensor-core path (tcgen05, TMA) needs b_stride_k == 1, K % 16 == 0,
+ * lda % 16 == 0, b_stride_n % 16 == 0 and 16-byte aligned a/b; other layouts
+ * run a CUDA-core kernel with identical results. */
+int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                 int64_t b_stride_n, int64_t M, int64_t N, int64_t K, const float* row_scale,
+                 const float* col_scale, const void* bias, int epilogue, const void* resid,
+                 int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
+                 const int64_t* indices, int64_t sequence, int gate_slot, void* out, int64_t ldo,
+                 void* stream);
+
+/* Raw int32 accumulators of the same GEMM (exactness checks of the integer path):
+ *   acc[m,n] = sum_k a[m,k] * b[k,n], acc row stride N. */
+int lr_int8_gemm_s32(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                     int64_t b_stride_n, int64_t M, int64_t N, int64_t K, int32_t* acc,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LR_W8A8_H */

@@ -1,0 +1,642 @@
+// HBM-bound row kernels of the W8A8 projection path (sm_100a):
+//   K1 quantize_rows, K2 int8_epilogue, K3/K4/K8 RMSNorm+adaLN(+quant)(+residual),
+//   K5 gated residual, K6/K7 SwiGLU(+quant).
+//
+// Layout: one 256-thread CTA per row. Thread t owns the 8-column chunks that
+// start at columns (c*256 + t)*8 for c = 0..C-1, so a warp reads 512
+// contiguous bytes of bf16 per chunk with 16-byte loads. A row is read from
+// HBM once and kept in registers as packed bf16 between the reduction passes
+// (every intermediate of these kernels is bf16-representable).
+#include <initializer_list>
+
+#include "lr_common.cuh"
+#include "lr_host.h"
+
+namespace lr {
+
+static __device__ unsigned int g_device_status = 0;
+
+__device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_device_status, bits); }
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kSpan = kThreads * 8;  // columns covered by one chunk sweep
+
+using bf16 = __nv_bfloat16;
+
+// Load the 8-column chunk starting at `col` of a row (zeros past `width`).
+// VEC: the chunk is 16-byte aligned and either fully inside or fully outside.
+template <bool VEC, bool STREAM>
+__device__ __forceinline__ uint4 load_chunk(const bf16* row, int64_t col, int64_t width) {
+  if (VEC) {
+    if (col < width) return STREAM ? ld_stream(row + col) : ld_keep(row + col);
+    return make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(row);
+    uint32_t h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = (col + e < width) ? p[col + e] : 0u;
+    return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
+                      h[6] | (h[7] << 16));
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store_chunk(bf16* row, int64_t col, int64_t width, const uint4& v) {
+  if (VEC) {
+    if (col < width) *reinterpret_cast<uint4*>(row + col) = v;
+  } else {
+    uint16_t* p = reinterpret_cast<uint16_t*>(row);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (col + e < width) p[col + e] = (uint16_t)(w[e >> 1] >> ((e & 1) * 16));
+  }
+}
+
+// Quantise eight values with scale s and store them as int8 at q[col..col+7].
+template <bool VEC>
+__device__ __forceinline__ void store_q8(int8_t* q, int64_t col, int64_t width, const float (&f)[8],
+                                         float s) {
+  int v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = quant_i8(f[e], s);
+  if (VEC) {
+    if (col < width) {
+      uint2 w;
+      w.x = (v[0] & 0xff) | ((v[1] & 0xff) << 8) | ((v[2] & 0xff) << 16) | ((uint32_t)(v[3] & 0xff) << 24);
+      w.y = (v[4] & 0xff) | ((v[5] & 0xff) << 8) | ((v[6] & 0xff) << 16) | ((uint32_t)(v[7] & 0xff) << 24);
+      *reinterpret_cast<uint2*>(q + col) = w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (col + e < width) q[col + e] = (int8_t)v[e];
+  }
+}
+
+// --------------------------------------------------------------------- K1
+template <int C, bool VEC>
+__global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const bf16* __restrict__ x,
+                                                                  int64_t row_stride, int width,
+                                                                  int8_t* __restrict__ q,
+                                                                  float* __restrict__ scales) {
+  __shared__ float red[kWarps];
+  const int64_t row = blockIdx.x;
+  const bf16* src = x + row * row_stride;
+  uint4 raw[C];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    raw[c] = load_chunk<VEC, true>(src, col, width);
+    float f[8];
+    unpack8(raw[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+  amax = block_max<kWarps>(amax, red);
+  const float s = row_scale_from_absmax(amax);
+  int8_t* dst = q + row * (int64_t)width;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    float f[8];
+    unpack8(raw[c], f);
+    store_q8<VEC>(dst, col, width, f, s);
+  }
+  if (threadIdx.x == 0) scales[row] = s;
+}
+
+// --------------------------------------------------------------- K3/K4/K8
+struct RmsArgs {
+  const bf16* x;
+  const bf16* update;  // K8 residual branch (may be null)
+  const bf16* weight;
+  float eps;
+  const bf16* table;  // may be null: no modulation, gate 1
+  int64_t table_rows, table_width;
+  const int64_t* indices;
+  int64_t sequence;
+  int hidden;
+  int shift_slot, scale_slot, gate_slot;
+  bf16* residual_out;
+  int8_t* q;
+  float* scales;
+  bf16* out;
+};
+
+// Resolve the adaLN table row of flattened row `row`; null if the table is
+// absent, or (with the status bit raised) if the index is out of range.
+__device__ __forceinline__ const bf16* table_row_ptr(const bf16* table, int64_t table_rows,
+                                                     int64_t table_width, const int64_t* indices,
+                                                     int64_t sequence, int64_t row, bool& bad) {
+  bad = false;
+  if (table == nullptr) return nullptr;
+  const int64_t tr = indices[row % sequence];
+  if (tr < 0 || tr >= table_rows) {
+    bad = true;
+    return nullptr;
+  }
+  return table + tr * table_width;
+}
+
+template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
+__global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
+  __shared__ float red[kWarps];
+  const int64_t row = blockIdx.x;
+  const int hidden = a.hidden;
+  bool bad;
+  const bf16* trow = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence,
+                                   row, bad);
+  if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
+  const bool have_table = trow != nullptr;
+  const bf16* src = a.x + row * (int64_t)hidden;
+
+  uint4 v[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    v[c] = load_chunk<VEC, true>(src, col, hidden);
+  }
+
+  if (RESID) {
+    // v = bf16(x + bf16(gate * update)); model/kernels.py:101-105
+    const bf16* upd = a.update + row * (int64_t)hidden;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      float xf[8], df[8], gf[8];
+      unpack8(v[c], xf);
+      unpack8(load_chunk<VEC, true>(upd, col, hidden), df);
+      if (have_table) {
+        unpack8(load_chunk<VEC, false>(trow + (int64_t)a.gate_slot * hidden, col, hidden), gf);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gf[e] = (a.table == nullptr) ? 1.0f : 0.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xf[e] = bf16r(__fadd_rn(xf[e], bf16r(__fmul_rn(gf[e], df[e]))));
+      v[c] = pack8(xf);
+      store_chunk<VEC>(a.residual_out + row * (int64_t)hidden, col, hidden, v[c]);
+    }
+  }
+
+  // Sum of squares in the fixed order: chunk by chunk, element by element.
+  float part = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float f[8];
+    unpack8(v[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part = __fadd_rn(part, __fmul_rn(f[e], f[e]));
+  }
+  const float ss = block_sum<kWarps>(part, red);
+  // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hidden), a.eps)));
+
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    float f[8], w[8];
+    unpack8(v[c], f);
+    unpack8(load_chunk<VEC, false>(a.weight, col, hidden), w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = bf16r(__fmul_rn(__fmul_rn(f[e], r), w[e]));
+    if (MOD && have_table) {
+      // m = bf16(bf16(n * bf16(1 + scale)) + shift)   (model/kernels.py:77-78,117-120)
+      float sc[8], sh[8];
+      unpack8(load_chunk<VEC, false>(trow + (int64_t)a.scale_slot * hidden, col, hidden), sc);
+      unpack8(load_chunk<VEC, false>(trow + (int64_t)a.shift_slot * hidden, col, hidden), sh);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        f[e] = bf16r(__fadd_rn(bf16r(__fmul_rn(f[e], bf16r(__fadd_rn(1.0f, sc[e])))), sh[e]));
+    }
+    if (QUANT) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    }
+    v[c] = pack8(f);
+  }
+
+  if (QUANT) {
+    amax = block_max<kWarps>(amax, red);
+    const float s = row_scale_from_absmax(amax);
+    int8_t* dst = a.q + row * (int64_t)hidden;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      float f[8];
+      unpack8(v[c], f);
+      store_q8<VEC>(dst, col, hidden, f, s);
+    }
+    if (threadIdx.x == 0) a.scales[row] = s;
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      store_chunk<VEC>(a.out + row * (int64_t)hidden, col, hidden, v[c]);
+    }
+  }
+}
+
+// --------------------------------------------------------------------- K5
+template <int C, bool VEC>
+__global__ void __launch_bounds__(kThreads) gated_residual_kernel(
+    const bf16* __restrict__ x, const bf16* __restrict__ y, const bf16* __restrict__ table,
+    int64_t table_rows, int64_t table_width, const int64_t* __restrict__ indices,
+    int64_t sequence, int hidden, int gate_slot, bf16* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  bool bad;
+  const bf16* trow = table_row_ptr(table, table_rows, table_width, indices, sequence, row, bad);
+  if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
+  const float gate_default = (table == nullptr) ? 1.0f : 0.0f;
+  const bf16* xr = x + row * (int64_t)hidden;
+  const bf16* yr = y + row * (int64_t)hidden;
+  uint4 xv[C], yv[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    xv[c] = load_chunk<VEC, true>(xr, col, hidden);
+    yv[c] = load_chunk<VEC, true>(yr, col, hidden);
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    float xf[8], yf[8], gf[8];
+    unpack8(xv[c], xf);
+    unpack8(yv[c], yf);
+    if (trow != nullptr) {
+      unpack8(load_chunk<VEC, false>(trow + (int64_t)gate_slot * hidden, col, hidden), gf);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gf[e] = gate_default;
+    }
+    // out = bf16(x + bf16(gate * y))   (model/kernels.py:146-153)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xf[e] = __fadd_rn(xf[e], bf16r(__fmul_rn(gf[e], yf[e])));
+    store_chunk<VEC>(out + row * (int64_t)hidden, col, hidden, pack8(xf));
+  }
+}
+
+// ------------------------------------------------------------------ K6/K7
+__device__ __forceinline__ float silu_bf16(float g) {
+  // bf16(g * sigmoid(g)), sigmoid(g) = 1 / (1 + exp(-g))   (model/kernels.py:165,177)
+  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+  return bf16r(__fmul_rn(g, sig));
+}
+
+template <int C, bool VEC, bool QUANT>
+__global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict__ projected,
+                                                          int inner, bf16* __restrict__ out,
+                                                          int8_t* __restrict__ q,
+                                                          float* __restrict__ scales) {
+  __shared__ float red[kWarps];
+  const int64_t row = blockIdx.x;
+  const bf16* value = projected + row * 2 * (int64_t)inner;
+  const bf16* gate = value + inner;
+  uint4 v[C];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    float vf[8], gf[8];
+    unpack8(load_chunk<VEC, true>(value, col, inner), vf);
+    unpack8(load_chunk<VEC, true>(gate, col, inner), gf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      vf[e] = bf16r(__fmul_rn(vf[e], silu_bf16(gf[e])));
+      if (QUANT) amax = fmaxf(amax, fabsf(vf[e]));
+    }
+    v[c] = pack8(vf);
+  }
+  if (QUANT) {
+    amax = block_max<kWarps>(amax, red);
+    const float s = row_scale_from_absmax(amax);
+    int8_t* dst = q + row * (int64_t)inner;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      float f[8];
+      unpack8(v[c], f);
+      store_q8<VEC>(dst, col, inner, f, s);
+    }
+    if (threadIdx.x == 0) scales[row] = s;
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      store_chunk<VEC>(out + row * (int64_t)inner, col, inner, v[c]);
+    }
+  }
+}
+
+// --------------------------------------------------------------------- K2
+// One CTA per row; 4 int32 accumulators per thread step.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) int8_epilogue_kernel(
+    const int32_t* __restrict__ acc, int64_t cols, const float* __restrict__ row_scale,
+    const float* __restrict__ col_scale, const bf16* __restrict__ bias, bf16* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  const float rs = row_scale[row];
+  const int32_t* ar = acc + row * cols;
+  uint16_t* orow = reinterpret_cast<uint16_t*>(out + row * cols);
+  const uint16_t* bb = reinterpret_cast<const uint16_t*>(bias);
+  for (int64_t col = (int64_t)threadIdx.x * 4; col < cols; col += (int64_t)kThreads * 4) {
+    int32_t a4[4];
+    if (VEC) {
+      const int4 t = __ldcs(reinterpret_cast<const int4*>(ar + col));
+      a4[0] = t.x; a4[1] = t.y; a4[2] = t.z; a4[3] = t.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a4[e] = (col + e < cols) ? ar[col + e] : 0;
+    }
+    uint16_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t n = col + e;
+      if (!VEC && n >= cols) { o[e] = 0; continue; }
+      float d = __fmul_rn(__fmul_rn(__int2float_rn(a4[e]), rs), col_scale[n]);
+      if (bias != nullptr) d = __fadd_rn(d, bf_bits(bb[n]));
+      o[e] = f2bf_bits(d);
+    }
+    if (VEC) {
+      uint2 w;
+      w.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+      w.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+      *reinterpret_cast<uint2*>(orow + col) = w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (col + e < cols) orow[col + e] = o[e];
+    }
+  }
+}
+
+// Smallest supported chunk count covering `width` columns, or -1.
+int pick_chunks(int64_t width) {
+  const int64_t need = (width + kSpan - 1) / kSpan;
+  const int options[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int c : options)
+    if (c >= need) return c;
+  return -1;
+}
+
+#define LR_CHUNK_DISPATCH(C, ...)                   \
+  switch (C) {                                      \
+    case 1: { constexpr int kC = 1; __VA_ARGS__; } break;   \
+    case 2: { constexpr int kC = 2; __VA_ARGS__; } break;   \
+    case 3: { constexpr int kC = 3; __VA_ARGS__; } break;   \
+    case 4: { constexpr int kC = 4; __VA_ARGS__; } break;   \
+    case 6: { constexpr int kC = 6; __VA_ARGS__; } break;   \
+    case 8: { constexpr int kC = 8; __VA_ARGS__; } break;   \
+    case 12: { constexpr int kC = 12; __VA_ARGS__; } break; \
+    default: { constexpr int kC = 16; __VA_ARGS__; } break; \
+  }
+
+constexpr int64_t kMaxRows = 0x7fffffff;
+
+}  // namespace
+
+int read_status_elementwise(unsigned int* bits, int clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess)
+    return launch_status("reading the device status");
+  if (clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)) != cudaSuccess)
+      return launch_status("clearing the device status");
+  }
+  *bits |= v;
+  return LR_OK;
+}
+
+}  // namespace lr
+
+using lr::bf16;
+using lr::kMaxRows;
+using lr::pick_chunks;
+
+extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
+                                int8_t* q, float* scales, void* stream) {
+  LR_REQUIRE(rows >= 0 && width > 0, "quantize_rows: invalid shape [%lld, %lld]", (long long)rows,
+             (long long)width);
+  LR_REQUIRE(row_stride >= width, "quantize_rows: row stride %lld < width %lld",
+             (long long)row_stride, (long long)width);
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(x && q && scales, "quantize_rows: null pointer");
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "quantize_rows: too many rows");
+  const int C = pick_chunks(width);
+  if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "quantize_rows: width %lld > 32768", (long long)width);
+  const bool vec = width % 8 == 0 && row_stride % 8 == 0 && lr::aligned(x, 16) && lr::aligned(q, 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bf16* xp = static_cast<const bf16*>(x);
+  LR_CHUNK_DISPATCH(C, {
+    if (vec)
+      lr::quantize_rows_kernel<kC, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales);
+    else
+      lr::quantize_rows_kernel<kC, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales);
+  });
+  return lr::launch_status("quantize_rows");
+}
+
+extern "C" int lr_int8_epilogue(const int32_t* acc, int64_t rows, int64_t cols,
+                                const float* row_scale, const float* col_scale, const void* bias,
+                                void* out, void* stream) {
+  LR_REQUIRE(rows >= 0 && cols > 0, "int8_epilogue: invalid shape");
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(acc && row_scale && col_scale && out, "int8_epilogue: null pointer");
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "int8_epilogue: too many rows");
+  const bool vec = cols % 4 == 0 && lr::aligned(acc, 16) && lr::aligned(out, 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec)
+    lr::int8_epilogue_kernel<true><<<(unsigned)rows, lr::kThreads, 0, s>>>(
+        acc, cols, row_scale, col_scale, static_cast<const bf16*>(bias), static_cast<bf16*>(out));
+  else
+    lr::int8_epilogue_kernel<false><<<(unsigned)rows, lr::kThreads, 0, s>>>(
+        acc, cols, row_scale, col_scale, static_cast<const bf16*>(bias), static_cast<bf16*>(out));
+  return lr::launch_status("int8_epilogue");
+}
+
+namespace {
+
+int check_table(const char* who, const void* table, int64_t table_rows, int64_t table_width,
+                const int64_t* indices, int64_t sequence, int64_t hidden, int slot_a, int slot_b,
+                int slot_c) {
+  LR_REQUIRE(sequence > 0, "%s: sequence must be positive", who);
+  if (table == nullptr) return LR_OK;
+  LR_REQUIRE(indices != nullptr, "%s: indices are required with a table", who);
+  LR_REQUIRE(table_rows > 0, "%s: empty adaLN table", who);
+  const int hi = slot_a > slot_b ? (slot_a > slot_c ? slot_a : slot_c) : (slot_b > slot_c ? slot_b : slot_c);
+  const int lo = slot_a < slot_b ? (slot_a < slot_c ? slot_a : slot_c) : (slot_b < slot_c ? slot_b : slot_c);
+  LR_REQUIRE(lo >= 0 && (int64_t)(hi + 1) * hidden <= table_width,
+             "%s: slot %d does not fit a table row of width %lld (hidden %lld)", who, hi,
+             (long long)table_width, (long long)hidden);
+  return LR_OK;
+}
+
+bool vec_ok(int64_t hidden, std::initializer_list<const void*> ptrs) {
+  if (hidden % 8) return false;
+  for (const void* p : ptrs)
+    if (p && !lr::aligned(p, 16)) return false;
+  return true;
+}
+
+}  // namespace
+
+static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, bool quant, bool vec,
+                      cudaStream_t s) {
+  const int C = pick_chunks(a.hidden);
+  if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln: hidden %d > 32768", a.hidden);
+#define LR_RMS(V, R, M, Q) lr::rms_mod_kernel<kC, V, R, M, Q><<<(unsigned)rows, lr::kThreads, 0, s>>>(a)
+#define LR_RMS_Q(V, R, M)  \
+  if (quant) LR_RMS(V, R, M, true); else LR_RMS(V, R, M, false)
+#define LR_RMS_M(V, R)     \
+  if (mod) { LR_RMS_Q(V, R, true); } else { LR_RMS_Q(V, R, false); }
+#define LR_RMS_R(V)        \
+  if (resid) { LR_RMS_M(V, true); } else { LR_RMS_M(V, false); }
+  LR_CHUNK_DISPATCH(C, {
+    if (vec) { LR_RMS_R(true); } else { LR_RMS_R(false); }
+  });
+#undef LR_RMS_R
+#undef LR_RMS_M
+#undef LR_RMS_Q
+#undef LR_RMS
+  return lr::launch_status("rms_adaln");
+}
+
+extern "C" int lr_rms_adaln(const void* x, const void* norm_weight, float eps, const void* table,
+                            int64_t table_rows, int64_t table_width, const int64_t* indices,
+                            int64_t sequence, int64_t rows, int64_t hidden, int shift_slot,
+                            int scale_slot, void* out, void* stream) {
+  LR_REQUIRE(rows >= 0 && hidden > 0, "rms_adaln: invalid shape");
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(x && norm_weight && out, "rms_adaln: null pointer");
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln: too many rows");
+  int st = check_table("rms_adaln", table, table_rows, table_width, indices, sequence, hidden,
+                       shift_slot, scale_slot, shift_slot);
+  if (st) return st;
+  lr::RmsArgs a{};
+  a.x = static_cast<const bf16*>(x);
+  a.weight = static_cast<const bf16*>(norm_weight);
+  a.eps = eps;
+  a.table = static_cast<const bf16*>(table);
+  a.table_rows = table_rows;
+  a.table_width = table_width;
+  a.indices = indices;
+  a.sequence = sequence;
+  a.hidden = (int)hidden;
+  a.shift_slot = shift_slot;
+  a.scale_slot = scale_slot;
+  a.out = static_cast<bf16*>(out);
+  const bool vec = vec_ok(hidden, {x, norm_weight, table, out}) && table_width % 8 == 0;
+  return rms_launch(a, rows, false, table != nullptr, false, vec, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lr_rms_adaln_quant_int8(const void* x, const void* norm_weight, float eps,
+                                       const void* table, int64_t table_rows, int64_t table_width,
+                                       const int64_t* indices, int64_t sequence, int64_t rows,
+                                       int64_t hidden, int shift_slot, int scale_slot,
+                                       const void* update, int gate_slot, void* residual_out,
+                                       int8_t* q, float* scales, void* stream) {
+  LR_REQUIRE(rows >= 0 && hidden > 0, "rms_adaln_quant_int8: invalid shape");
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(x && norm_weight && q && scales, "rms_adaln_quant_int8: null pointer");
+  LR_REQUIRE(update == nullptr || residual_out != nullptr,
+             "rms_adaln_quant_int8: residual_out is required with update");
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln_quant_int8: too many rows");
+  int st = check_table("rms_adaln_quant_int8", table, table_rows, table_width, indices, sequence,
+                       hidden, shift_slot, scale_slot, update ? gate_slot : shift_slot);
+  if (st) return st;
+  lr::RmsArgs a{};
+  a.x = static_cast<const bf16*>(x);
+  a.update = static_cast<const bf16*>(update);
+  a.weight = static_cast<const bf16*>(norm_weight);
+  a.eps = eps;
+  a.table = static_cast<const bf16*>(table);
+  a.table_rows = table_rows;
+  a.table_width = table_width;
+  a.indices = indices;
+  a.sequence = sequence;
+  a.hidden = (int)hidden;
+  a.shift_slot = shift_slot;
+  a.scale_slot = scale_slot;
+  a.gate_slot = gate_slot;
+  a.residual_out = static_cast<bf16*>(residual_out);
+  a.q = q;
+  a.scales = scales;
+  const bool vec = vec_ok(hidden, {x, norm_weight, table, update, residual_out}) &&
+                   (table == nullptr || table_width % 8 == 0) && lr::aligned(q, 8);
+  return rms_launch(a, rows, update != nullptr, table != nullptr, true, vec,
+                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lr_gated_residual(const void* x, const void* y, const void* table,
+                                 int64_t table_rows, int64_t table_width, const int64_t* indices,
+                                 int64_t sequence, int64_t rows, int64_t hidden, int gate_slot,
+                                 void* out, void* stream) {
+  LR_REQUIRE(rows >= 0 && hidden > 0, "gated_residual: invalid shape");
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(x && y && out, "gated_residual: null pointer");
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "gated_residual: too many rows");
+  int st = check_table("gated_residual", table, table_rows, table_width, indices, sequence, hidden,
+                       gate_slot, gate_slot, gate_slot);
+  if (st) return st;
+  const int C = pick_chunks(hidden);
+  if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "gated_residual: hidden > 32768");
+  const bool vec = vec_ok(hidden, {x, y, table, out}) && (table == nullptr || table_width % 8 == 0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bf16 *xp = static_cast<const bf16*>(x), *yp = static_cast<const bf16*>(y),
+             *tp = static_cast<const bf16*>(table);
+  bf16* op = static_cast<bf16*>(out);
+  LR_CHUNK_DISPATCH(C, {
+    if (vec)
+      lr::gated_residual_kernel<kC, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(
+          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op);
+    else
+      lr::gated_residual_kernel<kC, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(
+          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op);
+  });
+  return lr::launch_status("gated_residual");
+}
+
+static int swiglu_common(const char* who, const void* projected, int64_t rows, int64_t inner,
+                         void* out, int8_t* q, float* scales, void* stream) {
+  LR_REQUIRE(rows >= 0 && inner > 0, "%s: invalid shape", who);
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(projected != nullptr, "%s: null pointer", who);
+  if (rows > kMaxRows) return lr::set_error(LR_ERR_UNSUPPORTED, "%s: too many rows", who);
+  const int C = pick_chunks(inner);
+  if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "%s: inner width > 32768", who);
+  const bool quant = q != nullptr;
+  const bool vec = vec_ok(inner, {projected, out}) && (!quant || lr::aligned(q, 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bf16* p = static_cast<const bf16*>(projected);
+  bf16* o = static_cast<bf16*>(out);
+  LR_CHUNK_DISPATCH(C, {
+    if (vec) {
+      if (quant) lr::swiglu_kernel<kC, true, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+      else lr::swiglu_kernel<kC, true, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+    } else {
+      if (quant) lr::swiglu_kernel<kC, false, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+      else lr::swiglu_kernel<kC, false, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+    }
+  });
+  return lr::launch_status(who);
+}
+
+extern "C" int lr_swiglu(const void* projected, int64_t rows, int64_t inner, void* out,
+                         void* stream) {
+  if (rows > 0 && out == nullptr) return lr::set_error(LR_ERR_INVALID_ARGUMENT, "swiglu: null output");
+  return swiglu_common("swiglu", projected, rows, inner, out, nullptr, nullptr, stream);
+}
+
+extern "C" int lr_swiglu_quant_int8(const void* projected, int64_t rows, int64_t inner, int8_t* q,
+                                    float* scales, void* stream) {
+  if (rows > 0 && (q == nullptr || scales == nullptr))
+    return lr::set_error(LR_ERR_INVALID_ARGUMENT, "swiglu_quant_int8: null output");
+  return swiglu_common("swiglu_quant_int8", projected, rows, inner, nullptr, q, scales, stream);
+}

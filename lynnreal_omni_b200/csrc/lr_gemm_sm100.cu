@@ -1,0 +1,750 @@
+// INT8 GEMM with int32 accumulation and a fused bf16 epilogue on sm_100a.
+//
+// Tensor-core path (K10 of the reference, model/int8_gemm.py:117-150, rebuilt
+// for Blackwell rather than translated):
+//   * persistent kernel, one CTA per SM, grouped-M tile raster;
+//   * 128x256 output tiles, K staged 128 bytes at a time through a 4-deep
+//     shared-memory ring filled by TMA (128-byte swizzle, zero fill past the
+//     matrix edges — this is how ragged M/N/K tails are handled);
+//   * warp 0 issues TMA, one thread of warp 1 issues tcgen05.mma.kind::i8
+//     (M=128, N=256, K=32 per instruction) into a TMEM int32 accumulator;
+//   * two accumulators (2 x 256 TMEM columns) so warps 2-5 run the epilogue of
+//     tile i (tcgen05.ld -> fp32 scale/bias/GELU/gated residual -> bf16 stores)
+//     while the tensor core computes tile i+1;
+//   * every mbarrier wait is bounded (globaltimer); on timeout the kernel raises
+//     a device status bit, drains its own copies and MMAs, frees TMEM, returns.
+// No TMA multicast is used anywhere (the kernel may run on any GPU of a node).
+//
+// CUDA-core path: a shared-memory tiled kernel for operand layouts TMA cannot
+// address (non-K-major weights, unaligned strides). Integer accumulation is
+// exact in any order, so both paths produce identical bits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "lr_common.cuh"
+#include "lr_host.h"
+
+namespace lr {
+
+static __device__ unsigned int g_gemm_status = 0;
+
+namespace gemm {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes of K per stage (= int8 elements)
+constexpr int UK = 32;   // K per tcgen05.mma.kind::i8
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK;
+constexpr int B_STAGE = BN * BK;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
+constexpr int NUM_EPI_WARPS = 4;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int GROUP_M = 8;
+constexpr int BAR_BYTES = 256;
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * (A_STAGE + B_STAGE) + BAR_BYTES;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+enum Epi : int { kNone = 0, kGelu = 1, kGated = 2, kS32 = 3 };
+
+struct EpiArgs {
+  const float* row_scale;
+  const float* col_scale;
+  const bf16* bias;
+  bf16* out;
+  int64_t ldo;
+  const bf16* resid;
+  int64_t ldr;
+  const bf16* table;
+  int64_t table_rows, table_width;
+  const int64_t* indices;
+  int64_t sequence;
+  int gate_slot;
+  int32_t* acc_out;  // kS32: row stride N
+};
+
+// ------------------------------------------------------------ epilogue math
+__device__ __forceinline__ float dequant(int32_t acc, float rs, float cs) {
+  // (float(acc) * row_scale) * col_scale   (model/int8_gemm.py:145-146,193)
+  return __fmul_rn(__fmul_rn(__int2float_rn(acc), rs), cs);
+}
+
+// tanh-approximated GELU of a bf16 value, evaluated in fp32:
+//   0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;
+  const float kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// Final bf16 value of one output element. `d` already holds the dequantised
+// fp32 value including bias; `resid`/`gate` are used by kGated only.
+template <int EPI>
+__device__ __forceinline__ float finish(float d, float resid, float gate) {
+  if (EPI == kGelu) return gelu_tanh(bf16r(d));
+  if (EPI == kGated) return __fadd_rn(resid, bf16r(__fmul_rn(gate, bf16r(d))));
+  return d;
+}
+
+__device__ __forceinline__ const bf16* gate_row(const EpiArgs& ep, int64_t row, bool& bad) {
+  bad = false;
+  if (ep.table == nullptr) return nullptr;
+  const int64_t tr = ep.indices[row % ep.sequence];
+  if (tr < 0 || tr >= ep.table_rows) {
+    bad = true;
+    return nullptr;
+  }
+  return ep.table + tr * ep.table_width;  // the caller adds the gate slot offset
+}
+
+// ------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase of `bar` with parity `parity` to complete. Gives up when
+// another role has aborted, or after kWaitLimitNs (raising the status bit).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
+                                             volatile uint32_t* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1u;
+      atomicOr(&g_gemm_status, (unsigned)kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart.
+// Fields: start address>>4 [0,14), leading byte offset>>4 [16,30) (unused
+// for swizzled K-major, 1), stride byte offset>>4 [32,46), descriptor version
+// 1 at [46,48), swizzle mode 2 (128B) at [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) |
+         ((uint64_t)(1024u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+// Instruction descriptor for kind::i8: s32 accumulator [4,6)=2, signed A
+// [7,10)=1, signed B [10,13)=1, both K-major, N>>3 at [17,23), M>>4 at [24,29).
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Load 32 consecutive int32 TMEM columns of this thread's lane and wait for
+// them in the same asm block, so no consumer can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int span = GROUP_M * num_n;
+  const int group = t / span;
+  const int first = group * GROUP_M;
+  const int gsize = min(num_m - first, GROUP_M);
+  const int r = t - group * span;
+  mb = first + r % gsize;
+  nb = r / gsize;
+}
+
+// Epilogue of one 32-column chunk of one row, vectorised (all 32 columns valid).
+template <int EPI>
+__device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[32],
+                                                int64_t row, int col0, float rs,
+                                                const bf16* gate_ptr, bool have_gate) {
+  const float4* cs4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
+  float d[32];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 c = __ldg(cs4 + q);
+    d[4 * q + 0] = dequant((int32_t)acc[4 * q + 0], rs, c.x);
+    d[4 * q + 1] = dequant((int32_t)acc[4 * q + 1], rs, c.y);
+    d[4 * q + 2] = dequant((int32_t)acc[4 * q + 2], rs, c.z);
+    d[4 * q + 3] = dequant((int32_t)acc[4 * q + 3], rs, c.w);
+  }
+  if (ep.bias != nullptr) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float b[8];
+      unpack8(__ldg(b4 + q), b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d[8 * q + e] = __fadd_rn(d[8 * q + e], b[e]);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float o[8];
+    if (EPI == kGated) {
+      float x[8], g[8];
+      unpack8(*reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col0 + 8 * q), x);
+      if (have_gate) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(gate_ptr + col0 + 8 * q)), g);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = (ep.table == nullptr) ? 1.0f : 0.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = finish<EPI>(d[8 * q + e], x[e], g[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = finish<EPI>(d[8 * q + e], 0.0f, 0.0f);
+    }
+    dst[q] = pack8(o);
+  }
+}
+
+// Same, with per-column bounds (ragged N tail) and scalar accesses.
+template <int EPI>
+__device__ __forceinline__ void store_chunk_tail(const EpiArgs& ep, const uint32_t (&acc)[32],
+                                                 int64_t row, int col0, int N, float rs,
+                                                 const bf16* gate_ptr, bool have_gate) {
+  const uint16_t* bias = reinterpret_cast<const uint16_t*>(ep.bias);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int col = col0 + j;
+    if (col >= N) break;
+    if (EPI == kS32) {
+      ep.acc_out[row * (int64_t)N + col] = (int32_t)acc[j];
+      continue;
+    }
+    float d = dequant((int32_t)acc[j], rs, ep.col_scale[col]);
+    if (bias != nullptr) d = __fadd_rn(d, bf_bits(bias[col]));
+    float x = 0.0f, g = 0.0f;
+    if (EPI == kGated) {
+      x = bf_bits(reinterpret_cast<const uint16_t*>(ep.resid)[row * ep.ldr + col]);
+      g = have_gate ? bf_bits(reinterpret_cast<const uint16_t*>(gate_ptr)[col])
+                    : ((ep.table == nullptr) ? 1.0f : 0.0f);
+    }
+    reinterpret_cast<uint16_t*>(ep.out)[row * ep.ldo + col] = f2bf_bits(finish<EPI>(d, x, g));
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, int M, int N, int K,
+                   const EpiArgs ep) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sa = smem;                               // STAGES x [128 rows x 128 B]
+  uint8_t* sb = smem + STAGES * A_STAGE;            // STAGES x [256 rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES * B_STAGE);
+  uint64_t* full = bars;                            // TMA landed       (count 1 + tx)
+  uint64_t* empty = bars + STAGES;                  // MMA done reading (count 1)
+  uint64_t* tfull = bars + 2 * STAGES;              // accumulator ready (count 1)
+  uint64_t* tempty = bars + 2 * STAGES + NUM_ACC;   // accumulator drained (count 128)
+  uint64_t* drain = bars + 2 * STAGES + 2 * NUM_ACC;  // abort-path MMA drain (count 1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), NUM_EPI_WARPS);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&map_a);
+    prefetch_map(&map_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_expect_tx(fb, A_STAGE + B_STAGE);
+          tma_load_2d(smem_u32(sa + stage * A_STAGE), &map_a, fb, kb * BK, mb * BM);
+          tma_load_2d(smem_u32(sb + stage * B_STAGE), &map_b, fb, kb * BK, nb * BN);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Abort: let every copy this thread issued land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) {
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(smem_u32(&full[s]), issued_phase[s]) &&
+                   globaltimer() - t0 < kWaitLimitNs / 4) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+        if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + stage * A_STAGE);
+          const uint32_t b0 = smem_u32(sb + stage * B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / UK; ++kk)
+            mma_i8(d_tmem, sw128_desc(a0 + kk * UK), sw128_desc(b0 + kk * UK),
+                   (kb | kk) != 0 ? 1u : 0u);
+          mma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(smem_u32(&tfull[acc]));
+      }
+      if (!ok) {
+        // Abort: wait for the MMAs already issued before TMEM is released.
+        mma_commit(smem_u32(drain));
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue warps
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32) belong to this warp
+    int local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+      // One lane polls; the warp reconverges before the .sync.aligned TMEM loads.
+      int ok = 1;
+      if (lane == 0) ok = wait_bounded(smem_u32(&tfull[acc]), acc_phase, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
+      const bool row_ok = row < M;
+      float rs = 0.0f;
+      const bf16* gptr = nullptr;
+      bool have_gate = false;
+      if (row_ok) {
+        if (EPI != kS32) rs = ep.row_scale[row];
+        if (EPI == kGated && ep.table != nullptr) {
+          bool bad;
+          const bf16* g = gate_row(ep, row, bad);
+          if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+          if (g != nullptr) {
+            gptr = g + (int64_t)ep.gate_slot * N;
+            have_gate = true;
+          }
+        }
+      }
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + (uint32_t)(c * 32), r);
+        if (c == BN / 32 - 1) {
+          // All columns of this accumulator are in registers: hand it back.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+        }
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= N) continue;
+        if (EPI == kS32) {
+          if (col0 + 32 <= N && (N % 4) == 0) {
+            int4* dst = reinterpret_cast<int4*>(ep.acc_out + row * (int64_t)N + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2],
+                                 (int)r[4 * q + 3]);
+          } else {
+            store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
+          }
+        } else if (col0 + 32 <= N) {
+          store_chunk_vec<EPI>(ep, r, row, col0, rs, gptr, have_gate);
+        } else {
+          store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------- CUDA-core path
+constexpr int ST_M = 64, ST_N = 64, ST_K = 32;
+
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const int8_t* __restrict__ a, int64_t lda,
+                                                       const int8_t* __restrict__ b,
+                                                       int64_t bsk, int64_t bsn, int M, int N,
+                                                       int K, const EpiArgs ep) {
+  __shared__ int32_t As[ST_K][ST_M + 1];
+  __shared__ int32_t Bs[ST_K][ST_N + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * ST_M, n0 = (int64_t)blockIdx.x * ST_N;
+  int32_t acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += ST_K) {
+    for (int i = threadIdx.x; i < ST_M * ST_K; i += 256) {
+      const int mm = i / ST_K, kk = i % ST_K;
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < M && gk < K) ? (int32_t)a[gm * lda + gk] : 0;
+    }
+    for (int i = threadIdx.x; i < ST_N * ST_K; i += 256) {
+      const int nn = i / ST_K, kk = i % ST_K;
+      const int64_t gn = n0 + nn, gk = k0 + kk;
+      Bs[kk][nn] = (gn < N && gk < K) ? (int32_t)b[gk * bsk + gn * bsn] : 0;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < ST_K; ++kk)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += As[kk][ty * 4 + i] * Bs[kk][tx * 4 + j];
+    __syncthreads();
+  }
+  const uint16_t* bias = reinterpret_cast<const uint16_t*>(ep.bias);
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = m0 + ty * 4 + i;
+    if (row >= M) continue;
+    const bf16* gptr = nullptr;
+    bool have_gate = false;
+    if (EPI == kGated && ep.table != nullptr) {
+      bool bad;
+      const bf16* g = gate_row(ep, row, bad);
+      if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+      if (g != nullptr) gptr = g + (int64_t)ep.gate_slot * N, have_gate = true;
+    }
+    for (int j = 0; j < 4; ++j) {
+      const int64_t col = n0 + tx * 4 + j;
+      if (col >= N) continue;
+      if (EPI == kS32) {
+        ep.acc_out[row * (int64_t)N + col] = acc[i][j];
+        continue;
+      }
+      float d = dequant(acc[i][j], ep.row_scale[row], ep.col_scale[col]);
+      if (bias != nullptr) d = __fadd_rn(d, bf_bits(bias[col]));
+      float x = 0.0f, g = 0.0f;
+      if (EPI == kGated) {
+        x = bf_bits(reinterpret_cast<const uint16_t*>(ep.resid)[row * ep.ldr + col]);
+        g = have_gate ? bf_bits(reinterpret_cast<const uint16_t*>(gptr)[col])
+                      : ((ep.table == nullptr) ? 1.0f : 0.0f);
+      }
+      reinterpret_cast<uint16_t*>(ep.out)[row * ep.ldo + col] = f2bf_bits(finish<EPI>(d, x, g));
+    }
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D uint8 tensor map: `outer` rows of `inner` bytes, rows `stride` bytes
+// apart, box of box_outer rows x 128 bytes, 128-byte swizzle, zero fill.
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t stride,
+             uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(LR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LR_OK;
+}
+
+template <int EPI>
+int launch_tc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N, int K,
+              const EpiArgs& ep, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
+  if (st) return st;
+  st = make_map(&mb, b, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
+  if (st) return st;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM_BYTES) != cudaSuccess)
+      return launch_status("gemm: configuring shared memory");
+    configured[dev] = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_tc_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  return launch_status("int8 gemm (tcgen05)");
+}
+
+template <int EPI>
+int launch_simt(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int64_t bsn, int M,
+                int N, int K, const EpiArgs& ep, cudaStream_t stream) {
+  dim3 grid((N + ST_N - 1) / ST_N, (M + ST_M - 1) / ST_M);
+  if (grid.y > 65535) return set_error(LR_ERR_UNSUPPORTED, "gemm: too many rows for the CUDA-core path");
+  gemm_simt_kernel<EPI><<<grid, 256, 0, stream>>>(a, lda, b, bsk, bsn, M, N, K, ep);
+  return launch_status("int8 gemm (cuda cores)");
+}
+
+template <int EPI>
+int run(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int64_t bsn, int64_t M,
+        int64_t N, int64_t K, const EpiArgs& ep, bool out_vec_ok, cudaStream_t stream) {
+  const bool tc = bsk == 1 && K > 0 && lda % 16 == 0 && bsn % 16 == 0 && aligned(a, 16) &&
+                  aligned(b, 16) && out_vec_ok;
+  if (tc) return launch_tc<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream);
+  return launch_simt<EPI>(a, lda, b, bsk, bsn, (int)M, (int)N, (int)K, ep, stream);
+}
+
+}  // namespace gemm
+
+int read_status_gemm(unsigned int* bits, int clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess)
+    return launch_status("reading the gemm status");
+  if (clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(zero)) != cudaSuccess)
+      return launch_status("clearing the gemm status");
+  }
+  *bits |= v;
+  return LR_OK;
+}
+
+}  // namespace lr
+
+namespace {
+
+int check_gemm_shape(const char* who, const int8_t* a, int64_t lda, const int8_t* b,
+                     int64_t bsk, int64_t bsn, int64_t M, int64_t N, int64_t K) {
+  LR_REQUIRE(M >= 0 && N > 0 && K >= 0, "%s: invalid shape M=%lld N=%lld K=%lld", who,
+             (long long)M, (long long)N, (long long)K);
+  LR_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "%s: dimension too large", who);
+  LR_REQUIRE(lda >= K, "%s: lda %lld < K %lld", who, (long long)lda, (long long)K);
+  LR_REQUIRE(bsk >= 0 && bsn >= 0, "%s: negative weight strides", who);
+  LR_REQUIRE(M == 0 || (a != nullptr && b != nullptr), "%s: null operand", who);
+  return LR_OK;
+}
+
+}  // namespace
+
+extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                            int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
+                            const float* row_scale, const float* col_scale, const void* bias,
+                            int epilogue, const void* resid, int64_t ldr, const void* table,
+                            int64_t table_rows, int64_t table_width, const int64_t* indices,
+                            int64_t sequence, int gate_slot, void* out, int64_t ldo, void* stream) {
+  using namespace lr::gemm;
+  int st = check_gemm_shape("int8_gemm", a, lda, b, b_stride_k, b_stride_n, M, N, K);
+  if (st) return st;
+  if (M == 0) return LR_OK;
+  LR_REQUIRE(row_scale && col_scale && out, "int8_gemm: null scale or output pointer");
+  LR_REQUIRE(ldo >= N, "int8_gemm: ldo %lld < N %lld", (long long)ldo, (long long)N);
+  LR_REQUIRE(epilogue >= LR_EPI_NONE && epilogue <= LR_EPI_GATED_RESIDUAL,
+             "int8_gemm: unknown epilogue %d", epilogue);
+  EpiArgs ep{};
+  ep.row_scale = row_scale;
+  ep.col_scale = col_scale;
+  ep.bias = static_cast<const bf16*>(bias);
+  ep.out = static_cast<bf16*>(out);
+  ep.ldo = ldo;
+  // The tensor-core epilogue uses 16-byte accesses of out/bias/col_scale/resid and
+  // of the gate row (table + row*table_width + gate_slot*N): all must be aligned.
+  bool vec = lr::aligned(out, 16) && ldo % 8 == 0 && N % 8 == 0 && lr::aligned(col_scale, 16) &&
+             (bias == nullptr || lr::aligned(bias, 16));
+  if (epilogue == LR_EPI_GATED_RESIDUAL) {
+    LR_REQUIRE(resid != nullptr && ldr >= N, "int8_gemm: gated residual needs resid with ldr >= N");
+    LR_REQUIRE(sequence > 0, "int8_gemm: sequence must be positive");
+    if (table != nullptr) {
+      LR_REQUIRE(indices != nullptr && table_rows > 0, "int8_gemm: table needs indices and rows");
+      LR_REQUIRE(gate_slot >= 0 && (int64_t)(gate_slot + 1) * N <= table_width,
+                 "int8_gemm: gate slot %d does not fit table width %lld", gate_slot,
+                 (long long)table_width);
+    }
+    ep.resid = static_cast<const bf16*>(resid);
+    ep.ldr = ldr;
+    ep.table = static_cast<const bf16*>(table);
+    ep.table_rows = table_rows;
+    ep.table_width = table_width;
+    ep.indices = indices;
+    ep.sequence = sequence;
+    ep.gate_slot = gate_slot;
+    vec = vec && lr::aligned(resid, 16) && ldr % 8 == 0 &&
+          (table == nullptr || (lr::aligned(table, 16) && table_width % 8 == 0));
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (epilogue) {
+    case LR_EPI_GELU_TANH:
+      return run<kGelu>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+    case LR_EPI_GATED_RESIDUAL:
+      return run<kGated>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+    default:
+      return run<kNone>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+  }
+}
+
+extern "C" int lr_int8_gemm_s32(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                                int64_t b_stride_n, int64_t M, int64_t N, int64_t K, int32_t* acc,
+                                void* stream) {
+  using namespace lr::gemm;
+  int st = check_gemm_shape("int8_gemm_s32", a, lda, b, b_stride_k, b_stride_n, M, N, K);
+  if (st) return st;
+  if (M == 0) return LR_OK;
+  LR_REQUIRE(acc != nullptr, "int8_gemm_s32: null output");
+  EpiArgs ep{};
+  ep.acc_out = acc;
+  return run<kS32>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, lr::aligned(acc, 16),
+                   static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,277 @@
+"""CPU oracle of the LynnReal-Omni W8A8 projection path.
+
+TEST INFRASTRUCTURE ONLY. Only ``tests/``, ``__graft_entry__.smoke()`` and
+``bench.py`` (its CPU-baseline leg and its ``--impl reference`` arm) may import
+this module; the product path never does, and nothing here runs on a GPU.
+
+Each function restates one function of the reference (file:line cited; paths
+are relative to the reference project root) as plain CPU arithmetic:
+  * element-wise and row work in numpy float32, every product and sum rounded
+    on its own (the reference launches with ``enable_fp_fusion=False``), with
+    the reference's bf16 rounding points written out as ``bf16_round``;
+  * the integer GEMM through ``torch._int_mm`` on the CPU (exact int32), the
+    same library call the reference's own torch path makes.
+
+Reduction order. The only order-dependent quantity on the path is the
+RMSNorm sum of squares. ``sumsq_numpy`` is the order of the reference's Triton
+kernel when run by the Triton interpreter (``np.sum``); ``sumsq_tree`` is the
+fixed tree of the CUDA kernels (256 threads x 8-column chunks, then a warp
+butterfly, then a pairwise tree over 8 warps). All other steps are
+order-independent.
+
+Parity pinning: ``tests/test_oracle_golden.py`` checks every function here
+against golden vectors produced by the reference itself
+(``tests/golden/make_golden.py``: the reference's torch path and its Triton
+kernels under the Triton interpreter).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+F32 = np.float32
+
+# ---------------------------------------------------------------- bf16 helpers
+
+
+def bf16_bits(x) -> np.ndarray:
+    """Round float32 values to bf16 (nearest, ties to even); return uint16 bits."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    u = x.view(np.uint32).astype(np.uint64)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    nan = np.isnan(x)
+    if nan.any():
+        rounded = np.where(nan, (u >> 16) | 0x40, rounded)
+    return rounded.astype(np.uint16)
+
+
+def from_bf16_bits(bits) -> np.ndarray:
+    b = np.ascontiguousarray(bits, dtype=np.uint16)
+    return (b.astype(np.uint32) << 16).view(F32)
+
+
+def bf16_round(x) -> np.ndarray:
+    """bf(x): round to bf16 and back to float32."""
+    return from_bf16_bits(bf16_bits(x))
+
+
+def to_numpy_f32(t: torch.Tensor) -> np.ndarray:
+    """bf16/fp32 torch tensor -> float32 numpy array (exact)."""
+    return t.detach().to("cpu", torch.float32).contiguous().numpy()
+
+
+def to_torch_bf16(x: np.ndarray) -> torch.Tensor:
+    """float32 array of bf16-representable values -> bf16 torch tensor (exact)."""
+    bits = bf16_bits(x)
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+
+
+# ------------------------------------------------------------ K1 row quantiser
+
+
+def quantize_rows(x):
+    """Per-row symmetric int8 quantisation.
+
+    model/kernels.py:8-16 (``_quantize_rows_kernel``) and model/int8.py:66-67:
+    scale = max(max|x|, 1e-8) / 127 ; q = round_half_even(clamp(x / scale, -127, 127)).
+    Returns (int8 [rows, width], float32 [rows, 1]).
+    """
+    x = np.asarray(x, dtype=F32)
+    amax = np.max(np.abs(x), axis=-1, keepdims=True) if x.shape[-1] else np.zeros(x.shape[:-1] + (1,), F32)
+    scale = (np.maximum(amax, F32(1e-8)) / F32(127)).astype(F32)
+    q = np.rint(np.clip(x / scale, F32(-127), F32(127))).astype(np.int8)
+    return q, scale
+
+
+# ------------------------------------------------------- K10 GEMM + K2 epilogue
+
+
+def int8_gemm_s32(a: np.ndarray, b_kn: np.ndarray) -> np.ndarray:
+    """Exact int32 accumulators acc = a @ b (model/int8_gemm.py:192; model/int8.py:51)."""
+    at = torch.from_numpy(np.ascontiguousarray(a, dtype=np.int8))
+    bt = torch.from_numpy(np.ascontiguousarray(b_kn, dtype=np.int8))
+    return torch._int_mm(at, bt).numpy()
+
+
+def int8_epilogue(acc, row_scale, col_scale, bias=None) -> np.ndarray:
+    """bf16((float(acc) * row_scale) * col_scale + bias) as float32.
+
+    model/kernels.py:27-38 (``_int8_epilogue_kernel``), model/int8_gemm.py:188-196
+    (``_torch_matmul``), model/int8.py:55-58.
+    """
+    out = np.asarray(acc).astype(F32) * np.asarray(row_scale, F32).reshape(-1, 1)
+    out = out * np.asarray(col_scale, F32).reshape(1, -1)
+    if bias is not None:
+        out = out + np.asarray(bias, F32).reshape(1, -1)
+    return bf16_round(out)
+
+
+def int8_matmul(a, b_kn, row_scale, col_scale, bias=None) -> np.ndarray:
+    """INT8 GEMM with the fused bf16 epilogue (model/int8_gemm.py:117-150, 188-196)."""
+    return int8_epilogue(int8_gemm_s32(a, b_kn), row_scale, col_scale, bias)
+
+
+def gelu_tanh_bf16(x) -> np.ndarray:
+    """tanh-approximated GELU of bf16 values, result rounded to bf16.
+
+    The reference has no GELU; this is the module semantics of a bf16
+    ``Int8Linear`` output fed to ``torch.nn.functional.gelu(approximate="tanh")``.
+    """
+    t = to_torch_bf16(np.asarray(x, F32))
+    return to_numpy_f32(torch.nn.functional.gelu(t, approximate="tanh"))
+
+
+def int8_matmul_gelu(a, b_kn, row_scale, col_scale, bias=None) -> np.ndarray:
+    return gelu_tanh_bf16(int8_matmul(a, b_kn, row_scale, col_scale, bias))
+
+
+def int8_matmul_gated_residual(a, b_kn, row_scale, col_scale, bias, residual, table, indices,
+                               gate_slot) -> np.ndarray:
+    """Int8Linear output followed by the gated residual (model/int8.py:41-58 then
+    model/kernels.py:131-153): bf16(x + bf16(gate * bf16(dequant)))."""
+    y = int8_matmul(a, b_kn, row_scale, col_scale, bias)
+    return gated_residual(residual, y, table, indices, gate_slot)
+
+
+# ------------------------------------------------------------ reductions
+
+
+def sumsq_numpy(v: np.ndarray) -> np.ndarray:
+    """Row sum of squares in the order of the reference kernel run by the Triton
+    interpreter: ``np.sum`` over the kernel's power-of-two block
+    (``triton.next_power_of_2(hidden)``, model/kernels.py:270,287), zero padded."""
+    v = np.asarray(v, F32)
+    rows, width = v.shape
+    block = 1 << max(0, (width - 1).bit_length())
+    padded = np.zeros((rows, block), F32)
+    padded[:, :width] = v
+    return np.sum(padded * padded, axis=-1, dtype=F32)
+
+
+def sumsq_tree(v: np.ndarray, threads: int = 256) -> np.ndarray:
+    """Row sum of squares in the CUDA kernels' fixed order.
+
+    Thread t sums the squares of columns (c*threads + t)*8 + e, c outer, e inner;
+    the 32 lanes of a warp then add by an xor butterfly (16, 8, 4, 2, 1); the
+    warp sums are added pairwise, neighbours first.
+    """
+    v = np.asarray(v, F32)
+    rows, width = v.shape
+    span = threads * 8
+    chunks = max(1, -(-width // span))
+    padded = np.zeros((rows, chunks * span), F32)
+    padded[:, :width] = v
+    sq = (padded * padded).reshape(rows, chunks, threads, 8)
+    part = np.zeros((rows, threads), F32)
+    for c in range(chunks):
+        for e in range(8):
+            part = part + sq[:, c, :, e]
+    warps = threads // 32
+    lanes = part.reshape(rows, warps, 32)
+    idx = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        lanes = lanes + lanes[:, :, idx ^ off]
+    s = lanes[:, :, 0]
+    while s.shape[1] > 1:
+        s = s[:, 0::2] + s[:, 1::2]
+    return s[:, 0]
+
+
+# --------------------------------------------------- K3 / K4 / K8 row kernels
+
+
+def _table_rows(table, indices, rows: int, sequence: int):
+    table = np.asarray(table, F32)
+    idx = np.asarray(indices, np.int64).reshape(-1)
+    return table[idx[np.arange(rows) % sequence]]
+
+
+def _rms_modulate(v, weight, eps, table, indices, sequence, shift_slot, scale_slot, reduce):
+    rows, hidden = v.shape
+    ss = reduce(v)
+    r = (F32(1) / np.sqrt(ss / F32(hidden) + F32(eps))).astype(F32)
+    n = bf16_round((v * r[:, None]) * np.asarray(weight, F32)[None, :])
+    if table is None:
+        return n
+    t = _table_rows(table, indices, rows, sequence)
+    shift = t[:, shift_slot * hidden:(shift_slot + 1) * hidden]
+    scale = t[:, scale_slot * hidden:(scale_slot + 1) * hidden]
+    return bf16_round(bf16_round(n * bf16_round(F32(1) + scale)) + shift)
+
+
+def rms_adaln(x, weight, eps, table, indices, shift_slot, scale_slot, sequence=None,
+              reduce=sumsq_tree):
+    """RMSNorm + adaLN modulate, bf16 output (model/kernels.py:48-78, 260-272).
+
+    x: [rows, hidden] float32 (bf16 values); row r uses table[indices[r % sequence]].
+    """
+    v = np.asarray(x, F32)
+    seq = v.shape[0] if sequence is None else sequence
+    return _rms_modulate(v, weight, eps, table, indices, seq, shift_slot, scale_slot, reduce)
+
+
+def rms_adaln_quant_int8(x, weight, eps, table, indices, shift_slot, scale_slot, sequence=None,
+                         reduce=sumsq_tree):
+    """RMSNorm + adaLN modulate + per-row int8 quantisation
+    (model/kernels.py:81-128, 275-289). Returns (int8, float32 [rows, 1])."""
+    m = rms_adaln(x, weight, eps, table, indices, shift_slot, scale_slot, sequence, reduce)
+    return quantize_rows(m)
+
+
+def gated_residual(x, y, table, indices, gate_slot, sequence=None) -> np.ndarray:
+    """bf16(x + bf16(gate * y)) (model/kernels.py:131-153, 292-304); table None -> gate 1."""
+    x = np.asarray(x, F32)
+    y = np.asarray(y, F32)
+    rows, hidden = x.shape
+    if table is None:
+        gate = np.ones_like(x)
+    else:
+        seq = rows if sequence is None else sequence
+        gate = _table_rows(table, indices, rows, seq)[:, gate_slot * hidden:(gate_slot + 1) * hidden]
+    return bf16_round(x + bf16_round(gate * y))
+
+
+def residual_rms_quant(x, update, weight, eps, table, indices, sequence=None, reduce=sumsq_tree):
+    """Gated residual (slot 2) fused into the FFN prologue (slots 3, 4)
+    (model/kernels.py:101-105, 405-419). Returns (residual, int8, float32 [rows,1])."""
+    residual = gated_residual(x, update, table, indices, 2, sequence)
+    q, s = rms_adaln_quant_int8(residual, weight, eps, table, indices, 3, 4, sequence, reduce)
+    return residual, q, s
+
+
+# ---------------------------------------------------------------- K6 / K7
+
+
+def _silu_bf16(g):
+    sig = (F32(1) / (F32(1) + np.exp(-g))).astype(F32)
+    return bf16_round(g * sig)
+
+
+def swiglu(projected) -> np.ndarray:
+    """bf16(value * bf16(gate * sigmoid(gate))) over [rows, 2*inner]
+    (model/kernels.py:156-166, 307-315)."""
+    p = np.asarray(projected, F32)
+    inner = p.shape[-1] // 2
+    with np.errstate(over="ignore"):
+        return bf16_round(p[..., :inner] * _silu_bf16(p[..., inner:]))
+
+
+def swiglu_quant_int8(projected):
+    """SwiGLU then per-row int8 quantisation (model/kernels.py:169-185, 318-328)."""
+    return quantize_rows(swiglu(projected))
+
+
+# ---------------------------------------------------------- W8A8 linear
+
+
+def int8_linear_forward(x, weight_nk, weight_scale, bias=None) -> np.ndarray:
+    """Int8Linear.forward torch path (model/int8.py:60-68, 41-58): quantise the
+    rows, exact int32 GEMM with the [K, N] transpose view, bf16 epilogue."""
+    q, s = quantize_rows(x)
+    return int8_matmul(q, np.asarray(weight_nk, np.int8).T, s, np.asarray(weight_scale, F32).reshape(-1),
+                       bias)
+
+
+def quantize_weight(w):
+    """Int8Linear(source) weight quantisation (model/int8.py:9-13): per output row."""
+    return quantize_rows(np.asarray(w, F32))
