@@ -1,0 +1,453 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 W8A8 projection path: DiT-block tokens/s on 1..8 GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run. A step is one
+forward of the W8A8 path of one Flash-like DiT block (config 2: M=12240 tokens,
+D=6144, QKV 18432, FFN 24576 GELU-tanh, cross-attention Q/O with text K/V from a
+512x4096 context) on each GPU's own 12240-token latent; weights are replicated
+and no data crosses GPUs (weak scaling: the path is independent per token row).
+The timed region holds exactly K steps between a barrier and a device
+synchronize; the step time is the maximum over ranks of CUDA-event time.
+
+``--impl reference`` times the reference's own PyTorch CPU implementation of
+the same path (the torch port under oracle/) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W8A8 DiT-block tokens/s at 1/2/4/8 B200; INT8 GEMM TOPS vs tensor peak"
+NOMINAL_INT8_TOPS = 4500.0
+FALLBACK_BF16_BURST_TFLOPS = 1590.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--tokens", type=int, default=12240, help="token rows per GPU")
+    p.add_argument("--cpu-sample-rows", type=int, default=512)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload_config(args, world):
+    from lynnreal_omni_b200 import workloads as W
+    return {
+        "workload": "config2: one Flash-like DiT block, W8A8 projection path",
+        "model": "Flash-like DiT block (D=6144, 48x128 heads, FFN 24576 GELU-tanh)",
+        "tokens_per_gpu": args.tokens,
+        "global_batch": world,
+        "seq_len": args.tokens,
+        "global_tokens": args.tokens * world,
+        "projections": {"qkv": [W.HIDDEN, 3 * W.HIDDEN], "o": [W.HIDDEN, W.HIDDEN],
+                        "cross_q": [W.HIDDEN, W.HIDDEN], "cross_kv": [W.TEXT_DIM, 2 * W.HIDDEN],
+                        "cross_o": [W.HIDDEN, W.HIDDEN], "up": [W.HIDDEN, W.FFN], "down": [W.FFN, W.HIDDEN]},
+        "text_context": [W.TEXT_TOKENS, W.TEXT_DIM],
+        "attention": "cores stubbed (self-attn returns V, cross-attn returns Q): out of scope",
+        "parallelism": f"dp{world} (token rows per GPU, int8 weights replicated, no collective)",
+        "l2": "no flush: per-step working set (0.58 GB int8 weights + ~1.2 GB activations) >> 126 MB L2",
+    }
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return json.loads(path.read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def profile_traffic(kernel_tag: str):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary
+    (a line 'traffic_bytes_per_launch: N' in profiles/<kernel_tag>*.md), or None."""
+    for path in sorted((ROOT / "profiles").glob(f"{kernel_tag}*.md")):
+        for line in path.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip().split()[0]))
+                except ValueError:
+                    return None
+    return None
+
+
+class NvmlSampler:
+    """Reads SM clock, power and clock-event reasons of one GPU every 10 ms in a
+    thread during the timed region (NVML reads only; nothing is set)."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device: torch.device):
+        import threading
+        import pynvml
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        self.samples = []
+        self.stop_flag = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        n, h = self.nvml, self.handle
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM),
+                                     n.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                     n.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except n.NVMLError:
+                pass
+            time.sleep(0.01)
+
+    def start(self):
+        self.thread.start()
+        time.sleep(0.05)
+
+    def stop(self):
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        n = self.nvml
+        try:
+            max_sm = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+        except n.NVMLError:
+            max_sm = None
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": max_sm, "reasons": ["no samples"], "source": "nvml"}
+        hi = max(p for _, p, _ in self.samples)
+        loaded = [s for s in self.samples if s[1] >= 0.5 * hi] or self.samples
+        reasons = sorted({name for _, _, r in loaded for name, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(c for c, _, _ in loaded), "sm_max_mhz": max_sm,
+                "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded),
+                "power_w_max": hi, "source": "nvml, 10 ms"}
+
+
+def clock_sampler(device: torch.device, local_rank: int):
+    try:
+        return NvmlSampler(device)
+    except Exception:  # NVML unavailable: fall back to nvidia-smi
+        return ClockSampler(local_rank)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region (rank 0)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.index = visible.split(",")[local_rank] if visible else str(local_rank)
+        self.file = tempfile.NamedTemporaryFile(prefix="clocks", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.close()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        power = [num(r[3]) for r in rows if num(r[3]) is not None]
+        hi = max(power) if power else 0.0
+        loaded = [r for r in rows if num(r[3]) is not None and num(r[3]) >= 0.5 * hi] or rows
+        sm = [num(r[1]) for r in loaded if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": hi}
+
+
+def cpu_block_rate(weights_cpu, tokens: int, sample_rows: int, repeats: int = 3):
+    """Tokens/s of the reference's PyTorch CPU path on this host for a block of
+    `tokens` rows, from a bounded sample: the row-proportional part is timed on
+    `sample_rows` rows and extrapolated linearly; the text K/V projection (fixed
+    per block) is timed in full."""
+    from oracle import w8a8_torch as T
+    from lynnreal_omni_b200 import block
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, table, idx, ctx = block.make_inputs(sample_rows, seed=7)
+    x2 = x.view(sample_rows, -1)
+
+    def run_rows():
+        T.flash_block(x2, table, idx, ctx, weights_cpu)
+
+    def run_fixed():
+        q, s = T.quantize_rows(ctx)
+        T.int8_matmul(q, weights_cpu.cross_kv.weight.t(), s, weights_cpu.cross_kv.scale, weights_cpu.cross_kv.bias)
+
+    def med(fn):
+        fn()
+        ts = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+    t_all = med(run_rows)
+    t_fixed = med(run_fixed)
+    t_rows = max(t_all - t_fixed, 1e-9)
+    t_block = t_fixed + t_rows * tokens / sample_rows
+    return tokens / t_block, {"t_sample_s": t_all, "t_fixed_s": t_fixed, "t_block_s": t_block,
+                              "cores": torch.get_num_threads()}
+
+
+def run_reference(args, world):
+    """Rank 0: the reference's PyTorch CPU path, all host threads, bounded samples."""
+    from oracle import w8a8_torch as T
+    from lynnreal_omni_b200 import block
+    torch.set_num_threads(os.cpu_count() or 1)
+    weights = block.make_weights(seed=0)
+    x, table, idx, ctx = block.make_inputs(args.cpu_sample_rows, seed=7)
+    x2 = x.view(args.cpu_sample_rows, -1)
+
+    def fixed():
+        q, s = T.quantize_rows(ctx)
+        T.int8_matmul(q, weights.cross_kv.weight.t(), s, weights.cross_kv.scale, weights.cross_kv.bias)
+    fixed()
+    tf = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        fixed()
+        tf.append(time.perf_counter() - t0)
+    t_fixed = statistics.median(tf)
+    for _ in range(args.warmup):
+        T.flash_block(x2, table, idx, ctx, weights)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        T.flash_block(x2, table, idx, ctx, weights)
+        ts.append(time.perf_counter() - t0)
+    t_step = statistics.mean(ts)
+    t_block = t_fixed + max(t_step - t_fixed, 1e-9) * args.tokens / args.cpu_sample_rows
+    value = args.tokens / t_block
+    cores = torch.get_num_threads()
+    sample = (f"{args.cpu_sample_rows} of {args.tokens} token rows per step (row-proportional part "
+              f"extrapolated linearly to {args.tokens}; text K/V projection timed in full)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_block * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(args, 1),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample,
+                         "implementation": "reference PyTorch path (Int8Linear torch path + torch restatement "
+                                           "of the Triton kernels), oracle/w8a8_torch.py"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import torch.distributed as dist
+    from lynnreal_omni_b200 import block, _lib
+    from lynnreal_omni_b200 import workloads as W
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+
+    weights = block.make_weights(seed=0, device=dev)  # replicated: same seed on every rank
+    blk = block.FlashBlockW8A8(weights)
+    x, table, idx, ctx = block.make_inputs(args.tokens, seed=100 + rank, device=dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        blk(x, table, idx, ctx)
+    torch.cuda.synchronize()
+
+    sampler = clock_sampler(dev, local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        blk(x, table, idx, ctx, ffn_events=ffn[i])
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    elapsed_ms = start.elapsed_time(end)
+    ffn_ms = statistics.mean(a.elapsed_time(b) for a, b in ffn)
+    t = torch.tensor([elapsed_ms, ffn_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, ffn_ms = t.tolist()
+    status = _lib.device_status(clear=True)
+
+    # end to end through the public API: pinned host in, host out, every step
+    e2e = None
+    if not args.no_e2e:
+        x_h = x.cpu().pin_memory()
+        ctx_h = ctx.cpu().pin_memory()
+        out_h = torch.empty_like(x_h).pin_memory()
+        x_d, ctx_d = torch.empty_like(x), torch.empty_like(ctx)
+
+        def e2e_step():
+            x_d.copy_(x_h, non_blocking=True)
+            ctx_d.copy_(ctx_h, non_blocking=True)
+            h, _ = blk(x_d, table, idx, ctx_d)
+            out_h.copy_(h, non_blocking=True)
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([s2.elapsed_time(e2)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = te.item()
+        e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": x_h.numel() * 2 + ctx_h.numel() * 2,
+               "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e2e_ms / args.steps,
+               "api": "FlashBlockW8A8.forward (Int8Linear / kernels / int8_gemm over liblr_w8a8.so)"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # The dominant kernel runs in a timed region of ~0.1 s at full SM clock (see
+    # "clocks"), so its denominator is the burst figure: twice the measured
+    # burst bf16 rate (the B200 dense int8 rate is twice bf16 per clock).
+    peaks = measured_peaks()
+    bf16_burst = peaks.get("bf16_tflops")
+    peak = 2.0 * (bf16_burst if bf16_burst else FALLBACK_BF16_BURST_TFLOPS)
+    up_ops = 2.0 * args.tokens * W.FFN * W.HIDDEN
+    achieved = up_ops / (ffn_ms / 1e3) / 1e12
+    roofline = {
+        "kernel": "ffn_up int8 GEMM + GELU-tanh epilogue (gemm_tc_kernel<kGelu>), "
+                  f"M={args.tokens} K={W.HIDDEN} N={W.FFN}",
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s (int8)",
+        "frac": achieved / peak,
+        "peak_source": ("of measured: 2 x bf16_tflops burst in MEASURED_PEAKS.json (B200 dense int8 = 2 x bf16 "
+                        "per clock)" if bf16_burst else "of fallback: 2 x 1590 TFLOP/s bf16 burst"),
+        "peak_int8_at_sm_clock": 148 * 16384 * (clocks["sm_mhz"] if clocks and clocks.get("sm_mhz") else 1965.0)
+        * 1e6 / 1e12,
+        "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+        "algorithmic_ops_per_launch": up_ops,
+        "launch_ms": ffn_ms,
+        "traffic": profile_traffic("gemm_ffn_up"),
+    }
+    block_ops = 2.0 * args.tokens * W.HIDDEN * (3 * W.HIDDEN + 3 * W.HIDDEN + 2 * W.FFN) \
+        + 2.0 * W.TEXT_TOKENS * W.TEXT_DIM * 2 * W.HIDDEN
+    step_ms = elapsed_ms / args.steps
+    line = {
+        "metric": METRIC,
+        "value": world * args.tokens * args.steps / (elapsed_ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded; random-init int8 weights)",
+        "config": workload_config(args, world),
+        "block_tops": block_ops / (step_ms / 1e3) / 1e12,
+        "roofline": roofline,
+        "clocks": clocks,
+        "gpu_launches": block.LAUNCHES_PER_FORWARD * args.steps,
+        "device_status": status,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        wcpu = block.BlockWeights(**{k: (v.to("cpu") if hasattr(v, "to") else v)
+                                     for k, v in weights.__dict__.items()})
+        rate, info = cpu_block_rate(wcpu, args.tokens, args.cpu_sample_rows)
+        line["cpu_baseline"] = {
+            "value": rate, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+            "sample": (f"{args.cpu_sample_rows} of {args.tokens} token rows (row-proportional part "
+                       f"extrapolated linearly; text K/V projection timed in full)"),
+            "t_block_s": info["t_block_s"],
+        }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -4,14 +4,23 @@
 //   * every fp32 product and sum is rounded on its own (no FMA contraction),
 //     matching the reference's `enable_fp_fusion=False` launches
 //     (model/kernels.py:270,287,302; model/int8_gemm.py:243,260);
-//   * bf16 rounding points are round-to-nearest-even, written out as bf16r();
+//   * bf16 rounding points are round-to-nearest-even;
 //   * divisions and the RMS reciprocal square root are IEEE round-to-nearest
-//     (__fdiv_rn, __fsqrt_rn), so a CPU restatement reproduces them exactly;
-//   * float -> int8 quantisation rounds half to even (cvt.rni).
+//     (__fdiv_rn, __fsqrt_rn, __frcp_rn), so a CPU restatement reproduces them;
+//   * float -> int8 quantisation rounds half to even.
 //
-// Reductions use one fixed tree (see block_sum): thread partial sums in column
-// order, an xor butterfly inside each warp, then a fixed pairwise tree over the
-// warps. The CPU oracle restates the same tree.
+// Packed bf16 arithmetic. Where the reference computes an fp32 product or sum
+// of two bf16 values and rounds it to bf16, these kernels use one
+// mul.rn.bf16x2 / add.rn.bf16x2 per two elements. The results are identical:
+// the fp32 product of two bf16 values is exact, and rounding an fp32 sum to
+// bf16 equals rounding the exact sum once (fp32 carries more than 2*8+2
+// significand bits, so the double rounding is innocuous) — outside the
+// subnormal range, which activations of this path do not reach.
+//
+// Reductions use one fixed tree: per thread two running partials (even and odd
+// columns of its chunks) added at the end, then (block_sum) an xor butterfly
+// inside each warp and a pairwise tree over the warps. The CPU oracle restates
+// the same tree.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -20,14 +29,14 @@
 
 namespace lr {
 
-// Device-side status word. Kernels OR error bits into it instead of trapping;
-// the host reads and clears it with lr_device_status().
+// Device-side status bits. Kernels OR error bits into a status word instead of
+// trapping; the host reads and clears it with lr_device_status().
 enum : unsigned int {
   kDevErrTableIndex = 1u << 0,  // an adaLN index pointed outside the table
   kDevErrWaitTimeout = 1u << 1, // a bounded mbarrier wait gave up
 };
 
-// ---------------------------------------------------------------- bf16 helpers
+// ------------------------------------------------------- scalar bf16 helpers
 __device__ __forceinline__ float bf16r(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
@@ -38,36 +47,107 @@ __device__ __forceinline__ uint16_t f2bf_bits(float x) {
   __nv_bfloat16 h = __float2bfloat16_rn(x);
   return *reinterpret_cast<uint16_t*>(&h);
 }
-__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-  return (uint32_t)f2bf_bits(lo) | ((uint32_t)f2bf_bits(hi) << 16);
+
+// ------------------------------------------------------- packed bf16x2 helpers
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t w) {
+  return *reinterpret_cast<__nv_bfloat162*>(&w);
 }
-// Unpack eight bf16 values held in a 16-byte vector.
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) {
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Round two fp32 values to bf16 (nearest even) and pack them (lo, hi).
+__device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
+  return as_u32(__floats2bfloat162_rn(lo, hi));
+}
+// bf16(a * b) and bf16(a + b), element-wise on two packed values.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  return as_u32(__hmul2_rn(as_bf2(a), as_bf2(b)));
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  return as_u32(__hadd2_rn(as_bf2(a), as_bf2(b)));
+}
+// Running max of |a| over packed values (acc holds non-negative bf16 values).
+__device__ __forceinline__ uint32_t bamax2(uint32_t acc, uint32_t a) {
+  return as_u32(__hmax2(as_bf2(acc), as_bf2(a & 0x7fff7fffu)));
+}
+__device__ __forceinline__ float bamax_final(uint32_t acc) { return fmaxf(bf_lo(acc), bf_hi(acc)); }
+
+constexpr uint32_t kBf2One = 0x3f803f80u;  // (1.0, 1.0) in bf16x2
+
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   f[0] = bf_lo(v.x); f[1] = bf_hi(v.x);
   f[2] = bf_lo(v.y); f[3] = bf_hi(v.y);
   f[4] = bf_lo(v.z); f[5] = bf_hi(v.z);
   f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
 }
+// Round eight fp32 values to bf16 and pack them.
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 v;
-  v.x = pack_bf2(f[0], f[1]); v.y = pack_bf2(f[2], f[3]);
-  v.z = pack_bf2(f[4], f[5]); v.w = pack_bf2(f[6], f[7]);
-  return v;
+  return make_uint4(cvt2(f[0], f[1]), cvt2(f[2], f[3]), cvt2(f[4], f[5]), cvt2(f[6], f[7]));
+}
+__device__ __forceinline__ uint4 bmul8(const uint4& a, const uint4& b) {
+  return make_uint4(bmul2(a.x, b.x), bmul2(a.y, b.y), bmul2(a.z, b.z), bmul2(a.w, b.w));
+}
+__device__ __forceinline__ uint4 badd8(const uint4& a, const uint4& b) {
+  return make_uint4(badd2(a.x, b.x), badd2(a.y, b.y), badd2(a.z, b.z), badd2(a.w, b.w));
+}
+__device__ __forceinline__ uint32_t bamax8(uint32_t acc, const uint4& a) {
+  acc = bamax2(acc, a.x);
+  acc = bamax2(acc, a.y);
+  acc = bamax2(acc, a.z);
+  return bamax2(acc, a.w);
 }
 
-// Symmetric int8 quantisation of one value with an fp32 row scale:
-// RNE(clamp(v / s, -127, 127)), model/kernels.py:14,126 and model/int8.py:67.
-__device__ __forceinline__ int quant_i8(float v, float s) {
-  float q = __fdiv_rn(v, s);
-  q = fminf(fmaxf(q, -127.0f), 127.0f);
-  return __float2int_rn(q);
-}
+// ------------------------------------------------------------- quantisation
 // Row scale from a row absmax: max(absmax, 1e-8) / 127 (model/kernels.py:13,121-122).
 __device__ __forceinline__ float row_scale_from_absmax(float absmax) {
   return __fdiv_rn(fmaxf(absmax, 1.0e-8f), 127.0f);
 }
 
-// Read-only streaming loads/stores (bypass L1 allocation for one-touch data).
+// Scalar reference form: RNE(clamp(v / s, -127, 127)) (model/kernels.py:14,126).
+__device__ __forceinline__ int quant_i8(float v, float s) {
+  float q = __fdiv_rn(v, s);
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  return __float2int_rn(q);
+}
+
+// Eight bf16 values -> eight int8 (packed in a uint2), exactly
+// RNE(clamp(v / s, -127, 127)) with the IEEE quotient v / s.
+//   * s >= absmax/127 of the row, so |v / s| < 127.5 and the clamp never binds
+//     for finite values;
+//   * q0 = v * (1/s) (both IEEE-rounded) lies within 2^-16 of v / s for
+//     |v / s| < 128, so it rounds to the same integer unless it is within
+//     2^-14 of a half-integer; those (rare) rows redo the IEEE division;
+//   * rounding to an integer is the float add of 1.5*2^23 (exact RNE for
+//     |q| < 2^22), whose low mantissa byte is the two's-complement int8.
+__device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float f[8];
+  unpack8(v, f);
+  uint32_t b[8];
+  bool near_tie = false;
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 magic2 = make_float2(kMagic, kMagic);
+  const float2 nmagic2 = make_float2(-kMagic, -kMagic);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const float2 q0 = __fmul2_rn(make_float2(f[e], f[e + 1]), inv2);
+    const float2 t = __fadd2_rn(q0, magic2);
+    const float2 r = __fadd2_rn(t, nmagic2);
+    const float2 d = __fadd2_rn(q0, make_float2(-r.x, -r.y));
+    near_tie |= (fabsf(d.x) > 0.49993896484375f) | (fabsf(d.y) > 0.49993896484375f);  // 0.5 - 2^-14
+    b[e] = __float_as_uint(t.x);
+    b[e + 1] = __float_as_uint(t.y);
+  }
+  if (near_tie) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(__fdiv_rn(f[e], s), kMagic));
+  }
+  const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+  return make_uint2(lo, hi);
+}
+
+// Read-only streaming loads (bypass L1 allocation for one-touch data).
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return __ldcs(reinterpret_cast<const uint4*>(p));
 }

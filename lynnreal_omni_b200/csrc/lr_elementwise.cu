@@ -56,26 +56,19 @@ __device__ __forceinline__ void store_chunk(bf16* row, int64_t col, int64_t widt
   }
 }
 
-// Quantise eight values with scale s and store them as int8 at q[col..col+7].
+// Store eight int8 values (packed in a uint2) at q[col..col+7].
 template <bool VEC>
-__device__ __forceinline__ void store_q8(int8_t* q, int64_t col, int64_t width, const float (&f)[8],
-                                         float s) {
-  int v[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = quant_i8(f[e], s);
+__device__ __forceinline__ void store_q8(int8_t* q, int64_t col, int64_t width, const uint2& w) {
   if (VEC) {
-    if (col < width) {
-      uint2 w;
-      w.x = (v[0] & 0xff) | ((v[1] & 0xff) << 8) | ((v[2] & 0xff) << 16) | ((uint32_t)(v[3] & 0xff) << 24);
-      w.y = (v[4] & 0xff) | ((v[5] & 0xff) << 8) | ((v[6] & 0xff) << 16) | ((uint32_t)(v[7] & 0xff) << 24);
-      *reinterpret_cast<uint2*>(q + col) = w;
-    }
+    if (col < width) *reinterpret_cast<uint2*>(q + col) = w;
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      if (col + e < width) q[col + e] = (int8_t)v[e];
+      if (col + e < width) q[col + e] = (int8_t)((e < 4 ? w.x : w.y) >> (8 * (e & 3)));
   }
 }
+
+__device__ __forceinline__ uint4 splat8(uint32_t w) { return make_uint4(w, w, w, w); }
 
 // --------------------------------------------------------------------- K1
 template <int C, bool VEC>
@@ -87,25 +80,21 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const bf16* __r
   const int64_t row = blockIdx.x;
   const bf16* src = x + row * row_stride;
   uint4 raw[C];
-  float amax = 0.0f;
+  uint32_t amax2 = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
     raw[c] = load_chunk<VEC, true>(src, col, width);
-    float f[8];
-    unpack8(raw[c], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    amax2 = bamax8(amax2, raw[c]);
   }
-  amax = block_max<kWarps>(amax, red);
+  const float amax = block_max<kWarps>(bamax_final(amax2), red);
   const float s = row_scale_from_absmax(amax);
+  const float inv = __frcp_rn(s);
   int8_t* dst = q + row * (int64_t)width;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    float f[8];
-    unpack8(raw[c], f);
-    store_q8<VEC>(dst, col, width, f, s);
+    store_q8<VEC>(dst, col, width, quant8(raw[c], s, inv));
   }
   if (threadIdx.x == 0) scales[row] = s;
 }
@@ -163,75 +152,75 @@ __global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
   }
 
   if (RESID) {
-    // v = bf16(x + bf16(gate * update)); model/kernels.py:101-105
+    // v = bf16(x + bf16(gate * update))   (model/kernels.py:101-105)
     const bf16* upd = a.update + row * (int64_t)hidden;
+    const uint4 gate_default = splat8(a.table == nullptr ? kBf2One : 0u);
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      float xf[8], df[8], gf[8];
-      unpack8(v[c], xf);
-      unpack8(load_chunk<VEC, true>(upd, col, hidden), df);
-      if (have_table) {
-        unpack8(load_chunk<VEC, false>(trow + (int64_t)a.gate_slot * hidden, col, hidden), gf);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) gf[e] = (a.table == nullptr) ? 1.0f : 0.0f;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) xf[e] = bf16r(__fadd_rn(xf[e], bf16r(__fmul_rn(gf[e], df[e]))));
-      v[c] = pack8(xf);
+      const uint4 d = load_chunk<VEC, true>(upd, col, hidden);
+      const uint4 gt = have_table
+                           ? load_chunk<VEC, false>(trow + (int64_t)a.gate_slot * hidden, col, hidden)
+                           : gate_default;
+      v[c] = badd8(v[c], bmul8(gt, d));
       store_chunk<VEC>(a.residual_out + row * (int64_t)hidden, col, hidden, v[c]);
     }
   }
 
-  // Sum of squares in the fixed order: chunk by chunk, element by element.
-  float part = 0.0f;
+  // Sum of squares in the fixed order: two running partials per thread, over
+  // the even and the odd columns of its chunks (chunk by chunk, left to right),
+  // added at the end. A bf16 value's square is exact in fp32, so the fused
+  // multiply-add rounds exactly like the reference's separate multiply and add.
+  float2 part2 = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     float f[8];
     unpack8(v[c], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) part = __fadd_rn(part, __fmul_rn(f[e], f[e]));
+    for (int e = 0; e < 8; e += 2) {
+      const float2 x2 = make_float2(f[e], f[e + 1]);
+      part2 = __ffma2_rn(x2, x2, part2);
+    }
   }
-  const float ss = block_sum<kWarps>(part, red);
+  const float ss = block_sum<kWarps>(__fadd_rn(part2.x, part2.y), red);
   // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hidden), a.eps)));
 
-  float amax = 0.0f;
+  uint32_t amax2 = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
     float f[8], w[8];
     unpack8(v[c], f);
     unpack8(load_chunk<VEC, false>(a.weight, col, hidden), w);
+    // n = bf16((x * r) * w)   (model/kernels.py:65-68,106-108)
+    const float2 r2 = make_float2(r, r);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = bf16r(__fmul_rn(__fmul_rn(f[e], r), w[e]));
+    for (int e = 0; e < 8; e += 2) {
+      const float2 n2 = __fmul2_rn(__fmul2_rn(make_float2(f[e], f[e + 1]), r2), make_float2(w[e], w[e + 1]));
+      f[e] = n2.x;
+      f[e + 1] = n2.y;
+    }
+    uint4 m = pack8(f);
     if (MOD && have_table) {
       // m = bf16(bf16(n * bf16(1 + scale)) + shift)   (model/kernels.py:77-78,117-120)
-      float sc[8], sh[8];
-      unpack8(load_chunk<VEC, false>(trow + (int64_t)a.scale_slot * hidden, col, hidden), sc);
-      unpack8(load_chunk<VEC, false>(trow + (int64_t)a.shift_slot * hidden, col, hidden), sh);
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        f[e] = bf16r(__fadd_rn(bf16r(__fmul_rn(f[e], bf16r(__fadd_rn(1.0f, sc[e])))), sh[e]));
+      const uint4 sc = load_chunk<VEC, false>(trow + (int64_t)a.scale_slot * hidden, col, hidden);
+      const uint4 sh = load_chunk<VEC, false>(trow + (int64_t)a.shift_slot * hidden, col, hidden);
+      m = badd8(bmul8(m, badd8(splat8(kBf2One), sc)), sh);
     }
-    if (QUANT) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
-    }
-    v[c] = pack8(f);
+    if (QUANT) amax2 = bamax8(amax2, m);
+    v[c] = m;
   }
 
   if (QUANT) {
-    amax = block_max<kWarps>(amax, red);
+    const float amax = block_max<kWarps>(bamax_final(amax2), red);
     const float s = row_scale_from_absmax(amax);
+    const float inv = __frcp_rn(s);
     int8_t* dst = a.q + row * (int64_t)hidden;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      float f[8];
-      unpack8(v[c], f);
-      store_q8<VEC>(dst, col, hidden, f, s);
+      store_q8<VEC>(dst, col, hidden, quant8(v[c], s, inv));
     }
     if (threadIdx.x == 0) a.scales[row] = s;
   } else {
@@ -253,7 +242,7 @@ __global__ void __launch_bounds__(kThreads) gated_residual_kernel(
   bool bad;
   const bf16* trow = table_row_ptr(table, table_rows, table_width, indices, sequence, row, bad);
   if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
-  const float gate_default = (table == nullptr) ? 1.0f : 0.0f;
+  const uint4 gate_default = splat8(table == nullptr ? kBf2One : 0u);
   const bf16* xr = x + row * (int64_t)hidden;
   const bf16* yr = y + row * (int64_t)hidden;
   uint4 xv[C], yv[C];
@@ -266,27 +255,18 @@ __global__ void __launch_bounds__(kThreads) gated_residual_kernel(
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    float xf[8], yf[8], gf[8];
-    unpack8(xv[c], xf);
-    unpack8(yv[c], yf);
-    if (trow != nullptr) {
-      unpack8(load_chunk<VEC, false>(trow + (int64_t)gate_slot * hidden, col, hidden), gf);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) gf[e] = gate_default;
-    }
+    const uint4 gt = trow != nullptr
+                         ? load_chunk<VEC, false>(trow + (int64_t)gate_slot * hidden, col, hidden)
+                         : gate_default;
     // out = bf16(x + bf16(gate * y))   (model/kernels.py:146-153)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) xf[e] = __fadd_rn(xf[e], bf16r(__fmul_rn(gf[e], yf[e])));
-    store_chunk<VEC>(out + row * (int64_t)hidden, col, hidden, pack8(xf));
+    store_chunk<VEC>(out + row * (int64_t)hidden, col, hidden, badd8(xv[c], bmul8(gt, yv[c])));
   }
 }
 
 // ------------------------------------------------------------------ K6/K7
-__device__ __forceinline__ float silu_bf16(float g) {
-  // bf16(g * sigmoid(g)), sigmoid(g) = 1 / (1 + exp(-g))   (model/kernels.py:165,177)
-  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-  return bf16r(__fmul_rn(g, sig));
+__device__ __forceinline__ float silu(float g) {
+  // g * sigmoid(g), sigmoid(g) = 1 / (1 + exp(-g))   (model/kernels.py:165,177)
+  return __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
 }
 
 template <int C, bool VEC, bool QUANT>
@@ -299,30 +279,27 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict
   const bf16* value = projected + row * 2 * (int64_t)inner;
   const bf16* gate = value + inner;
   uint4 v[C];
-  float amax = 0.0f;
+  uint32_t amax2 = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    float vf[8], gf[8];
-    unpack8(load_chunk<VEC, true>(value, col, inner), vf);
+    float gf[8];
     unpack8(load_chunk<VEC, true>(gate, col, inner), gf);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      vf[e] = bf16r(__fmul_rn(vf[e], silu_bf16(gf[e])));
-      if (QUANT) amax = fmaxf(amax, fabsf(vf[e]));
-    }
-    v[c] = pack8(vf);
+    for (int e = 0; e < 8; ++e) gf[e] = silu(gf[e]);
+    // bf16(value * bf16(silu(gate)))
+    v[c] = bmul8(load_chunk<VEC, true>(value, col, inner), pack8(gf));
+    if (QUANT) amax2 = bamax8(amax2, v[c]);
   }
   if (QUANT) {
-    amax = block_max<kWarps>(amax, red);
+    const float amax = block_max<kWarps>(bamax_final(amax2), red);
     const float s = row_scale_from_absmax(amax);
+    const float inv = __frcp_rn(s);
     int8_t* dst = q + row * (int64_t)inner;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      float f[8];
-      unpack8(v[c], f);
-      store_q8<VEC>(dst, col, inner, f, s);
+      store_q8<VEC>(dst, col, inner, quant8(v[c], s, inv));
     }
     if (threadIdx.x == 0) scales[row] = s;
   } else {
@@ -354,24 +331,20 @@ __global__ void __launch_bounds__(kThreads) int8_epilogue_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) a4[e] = (col + e < cols) ? ar[col + e] : 0;
     }
-    uint16_t o[4];
+    float d[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int64_t n = col + e;
-      if (!VEC && n >= cols) { o[e] = 0; continue; }
-      float d = __fmul_rn(__fmul_rn(__int2float_rn(a4[e]), rs), col_scale[n]);
-      if (bias != nullptr) d = __fadd_rn(d, bf_bits(bb[n]));
-      o[e] = f2bf_bits(d);
+      const int64_t n = (col + e < cols) ? col + e : col;
+      // (float(acc) * row_scale) * col_scale + bias   (model/kernels.py:33-38)
+      d[e] = __fmul_rn(__fmul_rn(__int2float_rn(a4[e]), rs), col_scale[n]);
+      if (bias != nullptr) d[e] = __fadd_rn(d[e], bf_bits(bb[n]));
     }
     if (VEC) {
-      uint2 w;
-      w.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
-      w.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
-      *reinterpret_cast<uint2*>(orow + col) = w;
+      *reinterpret_cast<uint2*>(orow + col) = make_uint2(cvt2(d[0], d[1]), cvt2(d[2], d[3]));
     } else {
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        if (col + e < cols) orow[col + e] = o[e];
+        if (col + e < cols) orow[col + e] = f2bf_bits(d[e]);
     }
   }
 }

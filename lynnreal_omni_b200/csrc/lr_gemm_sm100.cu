@@ -43,7 +43,6 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int NUM_EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
-constexpr int GROUP_M = 8;
 constexpr int BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * (A_STAGE + B_STAGE) + BAR_BYTES;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -115,6 +114,12 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Arrive on the mbarrier at the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(bar), "r"(rank));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -214,12 +219,92 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  const int span = GROUP_M * num_n;
-  const int group = t / span;
-  const int first = group * GROUP_M;
-  const int gsize = min(num_m - first, GROUP_M);
-  const int r = t - group * span;
+// ------------------------------------------------ CTA-pair (cta_group::2) PTX
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  return remote;
+}
+// All threads of both CTAs; orders shared-memory writes (barrier init, TMEM
+// address) before any peer access, and keeps a CTA's shared memory alive
+// until its peer no longer reads it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool wait_bounded_cluster(uint32_t bar, uint32_t parity,
+                                                     volatile uint32_t* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1u;
+      atomicOr(&g_gemm_status, (unsigned)kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+// TMA load into this CTA's shared memory whose completion is signalled on an
+// mbarrier of either CTA of the pair (`bar` is a shared::cluster address).
+// No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+// Instruction descriptor of the pair MMA: M = 256 (128 rows per CTA), N = 256.
+constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(256 >> 4) << 24);
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdescPair), "r"(accumulate)
+      : "memory");
+}
+// Arrive (once the pair's prior MMAs complete) on the mbarrier at offset `bar`
+// in every CTA of `cta_mask`.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Grouped raster: `group` consecutive M-blocks are swept across all N-blocks
+// before the next group starts, so the group's A panel stays L2-resident while
+// B streams through once per group.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group, int& mb,
+                                            int& nb) {
+  const int span = group * num_n;
+  const int g = t / span;
+  const int first = g * group;
+  const int gsize = min(num_m - first, group);
+  const int r = t - g * span;
   mb = first + r % gsize;
   nb = r / gsize;
 }
@@ -253,22 +338,23 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     float o[8];
-    if (EPI == kGated) {
-      float x[8], g[8];
-      unpack8(*reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col0 + 8 * q), x);
-      if (have_gate) {
-        unpack8(__ldg(reinterpret_cast<const uint4*>(gate_ptr + col0 + 8 * q)), g);
-      } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = (ep.table == nullptr) ? 1.0f : 0.0f;
-      }
+    for (int e = 0; e < 8; ++e) o[e] = d[8 * q + e];
+    uint4 y = pack8(o);  // bf16(dequant)
+    if (EPI == kGelu) {
+      unpack8(y, o);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = finish<EPI>(d[8 * q + e], x[e], g[e]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = finish<EPI>(d[8 * q + e], 0.0f, 0.0f);
+      for (int e = 0; e < 8; ++e) o[e] = gelu_tanh(o[e]);
+      y = pack8(o);
+    } else if (EPI == kGated) {
+      // bf16(x + bf16(gate * bf16(dequant)))   (model/kernels.py:146-153)
+      const uint4 x = *reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col0 + 8 * q);
+      const uint32_t gd = (ep.table == nullptr) ? kBf2One : 0u;
+      const uint4 g = have_gate ? __ldg(reinterpret_cast<const uint4*>(gate_ptr + col0 + 8 * q))
+                                : make_uint4(gd, gd, gd, gd);
+      y = badd8(x, bmul8(g, y));
     }
-    dst[q] = pack8(o);
+    dst[q] = y;
   }
 }
 
@@ -298,10 +384,69 @@ __device__ __forceinline__ void store_chunk_tail(const EpiArgs& ep, const uint32
   }
 }
 
+// Drain one 128-row x 256-column accumulator of this warp's TMEM lanes:
+// tcgen05.ld 32 columns at a time, release the accumulator (arrive on
+// `release_bar`, in CTA `release_rank` of the cluster) once every column is
+// in registers, then run the epilogue and store.
+template <int EPI>
+__device__ __forceinline__ void drain_accumulator(const EpiArgs& ep, int M, int N, uint32_t tbase,
+                                                  int64_t row, int col_base, int lane,
+                                                  uint32_t release_bar, int release_rank,
+                                                  bool remote) {
+  const bool row_ok = row < M;
+  float rs = 0.0f;
+  const bf16* gptr = nullptr;
+  bool have_gate = false;
+  if (row_ok) {
+    if (EPI != kS32) rs = ep.row_scale[row];
+    if (EPI == kGated && ep.table != nullptr) {
+      bool bad;
+      const bf16* g = gate_row(ep, row, bad);
+      if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+      if (g != nullptr) {
+        gptr = g + (int64_t)ep.gate_slot * N;
+        have_gate = true;
+      }
+    }
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + (uint32_t)(c * 32), r);
+    if (c == BN / 32 - 1) {
+      // All columns of this accumulator are in registers: hand it back.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (remote)
+          mbar_arrive_cluster(release_bar, (uint32_t)release_rank);
+        else
+          mbar_arrive(release_bar);
+      }
+    }
+    const int col0 = col_base + c * 32;
+    if (!row_ok || col0 >= N) continue;
+    if (EPI == kS32) {
+      if (col0 + 32 <= N && (N % 4) == 0) {
+        int4* dst = reinterpret_cast<int4*>(ep.acc_out + row * (int64_t)N + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
+      } else {
+        store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
+      }
+    } else if (col0 + 32 <= N) {
+      store_chunk_vec<EPI>(ep, r, row, col0, rs, gptr, have_gate);
+    } else {
+      store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
-                   const __grid_constant__ CUtensorMap map_b, int M, int N, int K,
+                   const __grid_constant__ CUtensorMap map_b, int M, int N, int K, int group_m,
                    const EpiArgs ep) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -362,7 +507,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag)) {
             ok = false;
@@ -449,53 +594,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
-      const int64_t row = (int64_t)mb * BM + quad * 32 + lane;
-      const bool row_ok = row < M;
-      float rs = 0.0f;
-      const bf16* gptr = nullptr;
-      bool have_gate = false;
-      if (row_ok) {
-        if (EPI != kS32) rs = ep.row_scale[row];
-        if (EPI == kGated && ep.table != nullptr) {
-          bool bad;
-          const bf16* g = gate_row(ep, row, bad);
-          if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
-          if (g != nullptr) {
-            gptr = g + (int64_t)ep.gate_slot * N;
-            have_gate = true;
-          }
-        }
-      }
+      tile_coords(t, num_m, num_n, group_m, mb, nb);
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + (uint32_t)(c * 32), r);
-        if (c == BN / 32 - 1) {
-          // All columns of this accumulator are in registers: hand it back.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
-        }
-        const int col0 = nb * BN + c * 32;
-        if (!row_ok || col0 >= N) continue;
-        if (EPI == kS32) {
-          if (col0 + 32 <= N && (N % 4) == 0) {
-            int4* dst = reinterpret_cast<int4*>(ep.acc_out + row * (int64_t)N + col0);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2],
-                                 (int)r[4 * q + 3]);
-          } else {
-            store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
-          }
-        } else if (col0 + 32 <= N) {
-          store_chunk_vec<EPI>(ep, r, row, col0, rs, gptr, have_gate);
-        } else {
-          store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
-        }
-      }
+      drain_accumulator<EPI>(ep, M, N, tbase, (int64_t)mb * BM + quad * 32 + lane, nb * BN, lane,
+                             smem_u32(&tempty[acc]), 0, false);
     }
   }
 
@@ -504,6 +606,185 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------ CTA-pair tensor-core kernel
+// A cluster of two CTAs computes one 256x256 output tile: each CTA loads 128
+// rows of A and 128 rows (one N half) of B per 128-byte K step, the leader
+// (cluster rank 0) issues tcgen05.mma.cta_group::2 (M=256, N=256), and each CTA
+// drains its own 128-row accumulator from its TMEM. Per CTA a stage is 32 KB,
+// so six stages fit where the single-CTA kernel holds four.
+constexpr int STAGES2 = 6;
+constexpr int A2_STAGE = 128 * BK;
+constexpr int B2_STAGE = 128 * BK;
+constexpr size_t SMEM2_BYTES = 1024 + (size_t)STAGES2 * (A2_STAGE + B2_STAGE) + BAR_BYTES;
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
+                    const __grid_constant__ CUtensorMap map_b, int M, int N, int K, int group_m,
+                    const EpiArgs ep) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sa = smem;                       // STAGES2 x [128 rows x 128 B]
+  uint8_t* sb = smem + STAGES2 * A2_STAGE;  // STAGES2 x [128 rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES2 * B2_STAGE);
+  uint64_t* full = bars;                              // leader: both CTAs' copies landed
+  uint64_t* empty = bars + STAGES2;                   // pair MMA done reading (multicast)
+  uint64_t* tfull = bars + 2 * STAGES2;               // accumulator ready (multicast)
+  uint64_t* tempty = bars + 2 * STAGES2 + NUM_ACC;    // leader: both CTAs drained
+  uint64_t* drain = bars + 2 * STAGES2 + 2 * NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int num_m = (M + 255) / 256;
+  const int num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 2 * NUM_EPI_WARPS);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&map_a);
+    prefetch_map(&map_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued_any = false;
+      for (int t = cluster_id; t < tiles && ok; t += clusters) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          if (leader) mbar_expect_tx(fb, 2 * (A2_STAGE + B2_STAGE));
+          const uint32_t fb_leader = map_to_rank(fb, 0);
+          tma_load_2d_pair(smem_u32(sa + stage * A2_STAGE), &map_a, fb_leader, kb * BK,
+                           mb * 256 + (int)rank * 128);
+          tma_load_2d_pair(smem_u32(sb + stage * B2_STAGE), &map_b, fb_leader, kb * BK,
+                           nb * BN + (int)rank * 128);
+          issued_any = true;
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && issued_any) {
+        // Abort: copies signal the leader's barrier, so give the ones in flight
+        // a fixed grace period to land before this CTA can exit.
+        const unsigned long long t0 = globaltimer();
+        while (globaltimer() - t0 < 100000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------ MMA issuer (leader only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < tiles && ok; t += clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+        if (!wait_bounded_cluster(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + stage * A2_STAGE);
+          const uint32_t b0 = smem_u32(sb + stage * B2_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / UK; ++kk)
+            mma_i8_pair(d_tmem, sw128_desc(a0 + kk * UK), sw128_desc(b0 + kk * UK),
+                        (kb | kk) != 0 ? 1u : 0u);
+          mma_commit_pair(smem_u32(&empty[stage]), (uint16_t)0x3);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit_pair(smem_u32(&tfull[acc]), (uint16_t)0x3);
+      }
+      if (!ok) {
+        mma_commit_pair(smem_u32(drain), (uint16_t)0x1);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------- epilogue warps (both CTAs)
+    const int quad = warp & 3;
+    int local = 0;
+    for (int t = cluster_id; t < tiles; t += clusters, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+      int ok = 1;
+      if (lane == 0) ok = wait_bounded(smem_u32(&tfull[acc]), acc_phase, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(t, num_m, num_n, group_m, mb, nb);
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      drain_accumulator<EPI>(ep, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32 + lane,
+                             nb * BN, lane, smem_u32(&tempty[acc]), 0, true);
+    }
+  }
+
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(TMEM_COLS)
                  : "memory");
   }
@@ -607,6 +888,29 @@ int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
   return LR_OK;
 }
 
+// M-blocks per raster group: as many as keep the group's A panel (rows x K
+// bytes) within a quarter-to-half of the 126 MB L2, so the weights stream
+// from HBM about once per group.
+int raster_group(int block_rows, int num_m, int K) {
+  const int64_t budget = 48ll << 20;
+  int64_t g = budget / ((int64_t)block_rows * (K > 0 ? K : 1));
+  if (g < 1) g = 1;
+  return (int)(g < num_m ? g : num_m);
+}
+
+template <typename Kernel>
+int configure_smem(Kernel kernel, size_t bytes, bool (&done)[64]) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return LR_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+      cudaSuccess)
+    return launch_status("gemm: configuring shared memory");
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return LR_OK;
+}
+
+// Single-CTA tensor-core kernel: 128x256 tiles (used when M <= 128).
 template <int EPI>
 int launch_tc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N, int K,
               const EpiArgs& ep, cudaStream_t stream) {
@@ -615,19 +919,36 @@ int launch_tc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M,
   if (st) return st;
   st = make_map(&mb, b, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
   if (st) return st;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static bool configured[64] = {};
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM_BYTES) != cudaSuccess)
-      return launch_status("gemm: configuring shared memory");
-    configured[dev] = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  static bool done[64] = {};
+  st = configure_smem(gemm_tc_kernel<EPI>, SMEM_BYTES, done);
+  if (st) return st;
+  const int num_m = (M + BM - 1) / BM;
+  const int tiles = num_m * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tc_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  gemm_tc_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, M, N, K,
+                                                                  raster_group(BM, num_m, K), ep);
   return launch_status("int8 gemm (tcgen05)");
+}
+
+// CTA-pair tensor-core kernel: 256x256 tiles over clusters of two CTAs.
+template <int EPI>
+int launch_tc2(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N, int K,
+               const EpiArgs& ep, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 128);
+  if (st) return st;
+  st = make_map(&mb, b, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 128);
+  if (st) return st;
+  static bool done[64] = {};
+  st = configure_smem(gemm_tc2_kernel<EPI>, SMEM2_BYTES, done);
+  if (st) return st;
+  const int num_m = (M + 255) / 256;
+  const int tiles = num_m * ((N + BN - 1) / BN);
+  const int pairs = sm_count() / 2;
+  const int clusters = tiles < pairs ? tiles : pairs;
+  gemm_tc2_kernel<EPI><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(
+      ma, mb, M, N, K, raster_group(256, num_m, K), ep);
+  return launch_status("int8 gemm (tcgen05, CTA pair)");
 }
 
 template <int EPI>
@@ -644,6 +965,7 @@ int run(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int64_t bsn,
         int64_t N, int64_t K, const EpiArgs& ep, bool out_vec_ok, cudaStream_t stream) {
   const bool tc = bsk == 1 && K > 0 && lda % 16 == 0 && bsn % 16 == 0 && aligned(a, 16) &&
                   aligned(b, 16) && out_vec_ok;
+  if (tc && M > BM) return launch_tc2<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream);
   if (tc) return launch_tc<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream);
   return launch_simt<EPI>(a, lda, b, bsk, bsn, (int)M, (int)N, (int)K, ep, stream);
 }

@@ -1,0 +1,90 @@
+"""Run one kernel of the W8A8 path on synthetic inputs (for profilers and timing).
+
+    python -m lynnreal_omni_b200.profile_case gemm --m 2048 --k 6144 --n 24576 --epi gelu
+    python -m lynnreal_omni_b200.profile_case rms --m 12240 --d 6144
+    python -m lynnreal_omni_b200.profile_case quant --m 12240 --d 24576
+    python -m lynnreal_omni_b200.profile_case gated --m 12240 --d 6144
+
+Each case launches its kernel ``--iters`` times on cuda:0 and prints the mean
+CUDA-event time per launch and the algorithmic rate (TOP/s or GB/s).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from types import SimpleNamespace
+
+import torch
+
+
+def _time(fn, iters: int, warmup: int):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("case", choices=["gemm", "rms", "quant", "gated", "residual_rms"])
+    p.add_argument("--m", type=int, default=12240)
+    p.add_argument("--k", type=int, default=6144)
+    p.add_argument("--n", type=int, default=24576)
+    p.add_argument("--d", type=int, default=6144)
+    p.add_argument("--epi", choices=["none", "gelu", "gated"], default="none")
+    p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=1)
+    a = p.parse_args(argv)
+
+    from . import kernels as K
+    from .int8_gemm import int8_matmul, int8_matmul_gated_residual, int8_matmul_gelu
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {"case": a.case}
+    if a.case == "gemm":
+        A = torch.randint(-127, 128, (a.m, a.k), device=dev, dtype=torch.int8, generator=g)
+        B = torch.randint(-127, 128, (a.n, a.k), device=dev, dtype=torch.int8, generator=g).t()
+        rs = torch.rand(a.m, 1, device=dev, generator=g) / 127
+        cs = torch.rand(1, a.n, device=dev, generator=g) / 127
+        bias = (0.02 * torch.randn(a.n, device=dev, generator=g)).to(torch.bfloat16)
+        if a.epi == "gelu":
+            fn = lambda: int8_matmul_gelu(A, B, rs, cs, bias)  # noqa: E731
+        elif a.epi == "gated":
+            res = torch.randn(1, a.m, a.n, device=dev, generator=g).to(torch.bfloat16)
+            table = (0.1 * torch.randn(1, 6 * a.n, device=dev, generator=g)).to(torch.bfloat16)
+            idx = torch.zeros(a.m, dtype=torch.int64, device=dev)
+            fn = lambda: int8_matmul_gated_residual(A, B, rs, cs, bias, res, table, idx, 5)  # noqa: E731
+        else:
+            fn = lambda: int8_matmul(A, B, rs, cs, bias)  # noqa: E731
+        ms = _time(fn, a.iters, a.warmup)
+        out.update(m=a.m, k=a.k, n=a.n, epi=a.epi, ms=ms, tops=2.0 * a.m * a.n * a.k / (ms / 1e3) / 1e12,
+                   algorithmic_bytes=a.m * a.k + a.n * a.k + 2 * a.m * a.n + 4 * a.m + 6 * a.n)
+    else:
+        x = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)
+        table = (0.1 * torch.randn(1, 6 * a.d, device=dev, generator=g)).to(torch.bfloat16)
+        idx = torch.zeros(a.m, dtype=torch.int64, device=dev)
+        norm = SimpleNamespace(weight=(1 + 0.05 * torch.randn(a.d, device=dev, generator=g)).to(torch.bfloat16),
+                               eps=1e-6)
+        if a.case == "rms":
+            fn, per_elem = (lambda: K._rms_adaln_quant_int8(x, norm, table, idx, 0, 1)), 3
+        elif a.case == "quant":
+            fn, per_elem = (lambda: K.quantize_rows(x.view(a.m, a.d))), 3
+        elif a.case == "gated":
+            fn, per_elem = (lambda: K._gated_residual(x, y, table, idx, 2)), 6
+        else:
+            fn, per_elem = (lambda: K.residual_rms_quant(x, y, norm, table, idx)), 7
+        ms = _time(fn, a.iters, a.warmup)
+        nbytes = per_elem * a.m * a.d + 4 * a.m
+        out.update(m=a.m, d=a.d, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

