@@ -97,65 +97,18 @@ def profile_traffic(kernel_tag: str):
     return None
 
 
-class NvmlSampler:
-    """Reads SM clock, power and clock-event reasons of one GPU every 10 ms in a
-    thread during the timed region (NVML reads only; nothing is set)."""
-
-    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
-               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
-
-    def __init__(self, device: torch.device):
-        import threading
+def clock_sampler(device: torch.device, local_rank: int):
+    """NVML sampler in its own process; nvidia-smi if NVML is unavailable."""
+    try:
         import pynvml
         pynvml.nvmlInit()
-        self.nvml = pynvml
-        uuid = str(torch.cuda.get_device_properties(device).uuid)
-        self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-        self.samples = []
-        self.stop_flag = threading.Event()
-        self.thread = threading.Thread(target=self._run, daemon=True)
-
-    def _run(self):
-        n, h = self.nvml, self.handle
-        while not self.stop_flag.is_set():
-            try:
-                self.samples.append((n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM),
-                                     n.nvmlDeviceGetPowerUsage(h) / 1000.0,
-                                     n.nvmlDeviceGetCurrentClocksEventReasons(h)))
-            except n.NVMLError:
-                pass
-            time.sleep(0.01)
-
-    def start(self):
-        self.thread.start()
-        time.sleep(0.05)
-
-    def stop(self):
-        self.stop_flag.set()
-        self.thread.join(timeout=2)
-        n = self.nvml
-        try:
-            max_sm = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
-        except n.NVMLError:
-            max_sm = None
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": max_sm, "reasons": ["no samples"], "source": "nvml"}
-        hi = max(p for _, p, _ in self.samples)
-        loaded = [s for s in self.samples if s[1] >= 0.5 * hi] or self.samples
-        reasons = sorted({name for _, _, r in loaded for name, bit in self.REASONS.items() if r & bit})
-        return {"sm_mhz": statistics.median(c for c, _, _ in loaded), "sm_max_mhz": max_sm,
-                "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded),
-                "power_w_max": hi, "source": "nvml, 10 ms"}
+        from lynnreal_omni_b200.clocks import ClockSampler as NvmlSampler
+        return NvmlSampler(str(torch.cuda.get_device_properties(device).uuid))
+    except Exception:
+        return SmiSampler(local_rank)
 
 
-def clock_sampler(device: torch.device, local_rank: int):
-    try:
-        return NvmlSampler(device)
-    except Exception:  # NVML unavailable: fall back to nvidia-smi
-        return ClockSampler(local_rank)
-
-
-class ClockSampler:
+class SmiSampler:
     """nvidia-smi clocks/throttle sampling during the timed region (rank 0)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -340,38 +293,38 @@ def run_ours(args, rank, world, local):
     elapsed_ms, ffn_ms = t.tolist()
     status = _lib.device_status(clear=True)
 
-    # end to end through the public API: pinned host in, host out, every step
+    # end to end through the public API: every step copies its latent and text
+    # context from pinned host memory and its result back to pinned host memory;
+    # HostPipeline overlaps step i's compute with the copies of steps i+1 / i-1.
     e2e = None
     if not args.no_e2e:
-        x_h = x.cpu().pin_memory()
+        from lynnreal_omni_b200.pipeline import HostPipeline
+        x_h = [x.cpu().pin_memory() for _ in range(2)]
         ctx_h = ctx.cpu().pin_memory()
-        out_h = torch.empty_like(x_h).pin_memory()
-        x_d, ctx_d = torch.empty_like(x), torch.empty_like(ctx)
-
-        def e2e_step():
-            x_d.copy_(x_h, non_blocking=True)
-            ctx_d.copy_(ctx_h, non_blocking=True)
-            h, _ = blk(x_d, table, idx, ctx_d)
-            out_h.copy_(h, non_blocking=True)
-        for _ in range(2):
-            e2e_step()
+        out_h = [torch.empty_like(x_h[0]).pin_memory() for _ in range(2)]
+        pipe = HostPipeline(lambda xd, cd: blk(xd, table, idx, cd)[0], dev, [x_h[0], ctx_h])
+        ins = [[x_h[i & 1], ctx_h] for i in range(args.steps)]
+        outs = [out_h[i & 1] for i in range(args.steps)]
+        pipe.run(ins[:2], outs[:2])
         torch.cuda.synchronize()
         barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
-        for _ in range(args.steps):
-            e2e_step()
+        pipe.run(ins, outs)
         e2.record()
         torch.cuda.synchronize()
         barrier()
+        ok = torch.equal(out_h[(args.steps - 1) & 1], blk(x, table, idx, ctx)[0].cpu())
         te = torch.tensor([s2.elapsed_time(e2)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = te.item()
         e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": x_h.numel() * 2 + ctx_h.numel() * 2,
-               "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e2e_ms / args.steps,
-               "api": "FlashBlockW8A8.forward (Int8Linear / kernels / int8_gemm over liblr_w8a8.so)"}
+               "h2d_bytes_per_step": x_h[0].numel() * 2 + ctx_h.numel() * 2,
+               "d2h_bytes_per_step": out_h[0].numel() * 2, "ms_per_step": e2e_ms / args.steps,
+               "result_matches_device_path": ok,
+               "api": "HostPipeline over FlashBlockW8A8.forward (Int8Linear / kernels / int8_gemm over "
+                      "liblr_w8a8.so); pinned host input and output every step, copies overlapped with compute"}
 
     if rank != 0:
         if world > 1:
@@ -398,7 +351,7 @@ def run_ours(args, rank, world, local):
         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
         "algorithmic_ops_per_launch": up_ops,
         "launch_ms": ffn_ms,
-        "traffic": profile_traffic("gemm_ffn_up"),
+        "traffic": profile_traffic("gemm_ffn_up_m12240"),
     }
     block_ops = 2.0 * args.tokens * W.HIDDEN * (3 * W.HIDDEN + 3 * W.HIDDEN + 2 * W.FFN) \
         + 2.0 * W.TEXT_TOKENS * W.TEXT_DIM * 2 * W.HIDDEN

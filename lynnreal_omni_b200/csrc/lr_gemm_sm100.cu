@@ -72,13 +72,16 @@ __device__ __forceinline__ float dequant(int32_t acc, float rs, float cs) {
 }
 
 // tanh-approximated GELU of a bf16 value, evaluated in fp32:
-//   0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
+//   0.5 * x * (1 + tanh(u)),  u = sqrt(2/pi) * (x + 0.044715 * x^3),
+// computed as the identical x / (1 + exp(-2u)), which needs one exponential
+// and no cancellation in the negative tail (where 1 + tanh(u) loses all its
+// significant bits).
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float kBeta = 0.7978845608028654f;
+  const float kTwoBeta = 1.5957691216057308f;  // 2 * sqrt(2/pi)
   const float kKappa = 0.044715f;
   const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+  const float two_u = __fmul_rn(kTwoBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
+  return __fdividef(x, __fadd_rn(1.0f, __expf(-two_u)));
 }
 
 // Final bf16 value of one output element. `d` already holds the dequantised
