@@ -47,6 +47,11 @@ def parse_args():
     p.add_argument("--cpu-sample-rows", type=int, default=512)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", choices=["block", "stack"], default="block",
+                   help="block: config 2 per GPU (weak scaling); stack: config 4, 42 blocks x 3 denoiser "
+                        "steps on 64512 tokens sharded over the GPUs with a final all-gather")
+    p.add_argument("--layers", type=int, default=42)
+    p.add_argument("--stack-tokens", type=int, default=64512)
     return p.parse_args()
 
 
@@ -392,6 +397,116 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_stack(args, rank, world, local):
+    """Config 4: 42-block stack, 3 denoiser steps, 64512 tokens sharded by rows
+    over the GPUs, one NCCL all-gather of the bf16 output at the end of a step.
+    A step is one full stack forward (every denoiser step through every block)."""
+    import torch.distributed as dist
+    from lynnreal_omni_b200 import _lib, stack as S
+    from lynnreal_omni_b200 import workloads as W
+    from lynnreal_omni_b200.parallel import shard_bounds
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    _lib.load()
+    total = args.stack_tokens
+    start_row, stop_row = shard_bounds(total, world, rank)
+    m = stop_row - start_row
+    model = S.FlashStackW8A8(args.layers, dev, seed=0)
+    g = W.generator(100 + rank, dev)
+    x_local = torch.randn(1, m, W.HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    ctx = torch.randn(W.TEXT_TOKENS, W.TEXT_DIM, generator=g, device=dev).to(torch.bfloat16)
+    idx = torch.zeros(m, dtype=torch.int64, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step(ev=None):
+        return model.sharded_forward(x_local, total, world, rank, idx, ctx, ffn_events=ev)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = clock_sampler(dev, local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(args.steps):
+        out = step(ffn[i])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    t = torch.tensor([t0.elapsed_time(t1), statistics.mean(a.elapsed_time(b) for a, b in ffn)], device=dev,
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, ffn_ms = t.tolist()
+    status = _lib.device_status(clear=True)
+
+    # end to end: the latent rows from pinned host memory in, the gathered output back
+    x_h = x_local.cpu().pin_memory()
+    out_h = torch.empty((total, W.HIDDEN), dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x_local)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x_d.copy_(x_h, non_blocking=True)
+        res = model.sharded_forward(x_d, total, world, rank, idx, ctx)
+        out_h.copy_(res.view(total, W.HIDDEN) if world > 1 else res.view(-1, W.HIDDEN), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    passes = S.DENOISER_STEPS * args.layers
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = 2.0 * (peaks.get("bf16_tflops") or FALLBACK_BF16_BURST_TFLOPS)
+        up_ops = 2.0 * m * W.FFN * W.HIDDEN
+        achieved = up_ops / (ffn_ms / 1e3) / 1e12
+        line = {
+            "metric": METRIC,
+            "value": total * passes * args.steps / (elapsed_ms / 1e3),
+            "unit": "tokens/s (block-token passes: tokens x blocks x denoiser steps)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; random-init int8 weights)",
+            "config": {"workload": "config4: 42-block Flash-like stack, 3 denoiser steps, tokens sharded by rows, "
+                                   "final NCCL all-gather of the bf16 output",
+                       "model": f"{args.layers} x Flash-like DiT block (D=6144, FFN 24576 GELU-tanh)",
+                       "global_tokens": total, "tokens_per_gpu": m, "layers": args.layers,
+                       "denoiser_steps": S.DENOISER_STEPS, "global_batch": 1, "seq_len": total,
+                       "parallelism": f"dp{world} over token rows, weights replicated, all-gather at the end",
+                       "l2": "no flush: 24.4 GB of weights streamed per denoiser step"},
+            "latent_tokens_per_s": total * S.DENOISER_STEPS * args.steps / (elapsed_ms / 1e3),
+            "roofline": {"kernel": f"ffn_up int8 GEMM + GELU (gemm_tc2_kernel<kGelu>), M={m} K={W.HIDDEN} N={W.FFN}",
+                         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s (int8)",
+                         "frac": achieved / peak, "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+                         "launch_ms": ffn_ms, "traffic": None},
+            "clocks": clocks,
+            "gpu_launches": model.launches_per_forward() * args.steps,
+            "device_status": status,
+            "e2e": {"value": total * passes * args.steps / (te.item() / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x_h.numel() * 2, "d2h_bytes_per_step": out_h.numel() * 2,
+                    "ms_per_step": te.item() / args.steps},
+        }
+        print(json.dumps(line), flush=True)
+    del out
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
@@ -399,7 +514,10 @@ def main():
         if rank == 0:
             run_reference(args, world)
         return
-    run_ours(args, rank, world, local)
+    if args.workload == "stack":
+        run_stack(args, rank, world, local)
+    else:
+        run_ours(args, rank, world, local)
 
 
 if __name__ == "__main__":

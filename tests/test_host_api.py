@@ -1,0 +1,124 @@
+"""CPU tests of the C ABI library and of the host-side API (no GPU needed)."""
+from __future__ import annotations
+
+import ctypes
+import json
+from pathlib import Path
+from types import SimpleNamespace
+
+import pytest
+import torch
+from torch import nn
+
+from lynnreal_omni_b200 import _lib
+from lynnreal_omni_b200.int8 import Int8Linear, quantize_transformer
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_library_exports_every_declared_symbol():
+    declared = _lib.header_symbols()
+    assert len(declared) >= 12
+    lib = _lib.load()
+    missing = [name for name in declared if not hasattr(lib, name)]
+    assert not missing, missing
+    assert set(declared) == set(_lib.SIGNATURES), "binding and header disagree"
+
+
+def test_library_version_and_error_path_without_gpu():
+    lib = _lib.load()
+    assert lib.lr_version() >= 100
+    # argument validation happens on the host, before any CUDA call
+    st = lib.lr_quantize_rows(None, 4, 0, 0, None, None, None)
+    assert st == _lib.LR_ERR_INVALID_ARGUMENT
+    assert b"invalid shape" in lib.lr_last_error()
+    st = lib.lr_int8_gemm(None, 4, None, 1, 8, 4, 8, 16, None, None, None, 0, None, 0, None, 0, 0, None, 1, 0,
+                          None, 8, None)
+    assert st == _lib.LR_ERR_INVALID_ARGUMENT
+    with pytest.raises(ValueError):
+        _lib.check(st, "int8_matmul")
+
+
+def test_empty_rows_are_a_no_op():
+    lib = _lib.load()
+    assert lib.lr_quantize_rows(None, 0, 64, 64, None, None, None) == _lib.LR_OK
+    assert lib.lr_gated_residual(None, None, None, 0, 0, None, 1, 0, 64, 0, None, None) == _lib.LR_OK
+
+
+def test_ops_refuse_cpu_tensors():
+    from lynnreal_omni_b200 import kernels as K
+    with pytest.raises(ValueError):
+        K.quantize_rows(torch.zeros(2, 8, dtype=torch.bfloat16))
+
+
+def test_int8_linear_contract():
+    with pytest.raises(ValueError):
+        Int8Linear(nn.Linear(8, 4), gemm="cublas")
+    with pytest.raises(ValueError):
+        Int8Linear.from_packed(torch.zeros(4, 8), torch.ones(4, 1))
+    with pytest.raises(ValueError):
+        Int8Linear.from_packed(torch.zeros(4, 8, dtype=torch.int8), torch.ones(4))
+    layer = Int8Linear.from_packed(torch.zeros(4, 8, dtype=torch.int8), torch.ones(4, 1))
+    assert layer.in_features == 8 and layer.out_features == 4 and layer.gemm == "triton"
+    assert layer.weight_int8.shape == (8, 4) and layer.weight_int8.stride() == (1, 8)
+    assert layer.weight.dtype == torch.bfloat16 and layer.weight.numel() == 0
+    assert not layer.fused_ops
+
+
+def test_int8_linear_torch_backend_on_cpu_matches_oracle():
+    """gemm="torch" is the reference's own path; it runs on the CPU too."""
+    import numpy as np
+    from oracle import w8a8_oracle as O
+    from lynnreal_omni_b200 import workloads
+    x, pl = workloads.config0(seed=8, m=21, k=256, n=72)
+    layer = Int8Linear.from_packed(pl.weight, pl.scale, pl.bias, gemm="torch")
+    y = layer(x.view(1, 21, 256))
+    ref = O.int8_linear_forward(O.to_numpy_f32(x), pl.weight.numpy(), pl.scale.numpy(), O.to_numpy_f32(pl.bias))
+    assert y.shape == (1, 21, 72)
+    np.testing.assert_array_equal(O.bf16_bits(O.to_numpy_f32(y).reshape(21, 72)), O.bf16_bits(ref))
+
+
+class _Attn(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.to_q, self.to_k, self.to_v = nn.Linear(d, d), nn.Linear(d, d), nn.Linear(d, d, bias=False)
+        self.to_out = nn.ModuleList([nn.Linear(d, d), nn.Dropout(0.0)])
+
+
+class _Proj(nn.Module):
+    def __init__(self, d, f):
+        super().__init__()
+        self.proj = nn.Linear(d, f)
+
+
+class _Block(nn.Module):
+    def __init__(self, d, f):
+        super().__init__()
+        self.attn = _Attn(d)
+        self.ff = SimpleNamespace(net=nn.ModuleList([_Proj(d, f), nn.Dropout(0.0), nn.Linear(f, d)]))
+
+
+def test_quantize_transformer_matches_reference_report():
+    golden = json.loads((ROOT / "tests" / "golden" / "quantize_transformer.json").read_text())
+    torch.manual_seed(5)
+    model = SimpleNamespace(transformer_blocks=[_Block(32, 64) for _ in range(4)])
+    report = quantize_transformer(model, protected_edges=1, gemm="torch")
+    assert report == golden
+    b1 = model.transformer_blocks[1]
+    assert isinstance(b1.attn.to_qkv, Int8Linear) and b1.attn.to_qkv.out_features == 96
+    assert isinstance(model.transformer_blocks[0].attn.to_qkv, nn.Linear)
+    with pytest.raises(ValueError):
+        quantize_transformer(SimpleNamespace(transformer_blocks=[_Block(8, 8)]), protected_edges=1)
+
+
+def test_c_header_compiles_as_c():
+    """include/lr_w8a8.h is plain C."""
+    import subprocess
+    import tempfile
+    src = '#include "lr_w8a8.h"\nint main(void){ return lr_version() < 0; }\n'
+    with tempfile.TemporaryDirectory() as d:
+        c = Path(d) / "t.c"
+        c.write_text(src)
+        r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-I", str(ROOT / "include"),
+                            str(c)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
