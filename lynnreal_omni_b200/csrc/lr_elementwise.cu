@@ -8,6 +8,8 @@
 // HBM once and kept in registers as packed bf16 between the reduction passes
 // (every intermediate of these kernels is bf16-representable).
 #include <initializer_list>
+#include <mutex>
+#include <unordered_map>
 
 #include "lr_common.cuh"
 #include "lr_host.h"
@@ -70,33 +72,63 @@ __device__ __forceinline__ void store_q8(int8_t* q, int64_t col, int64_t width, 
 
 __device__ __forceinline__ uint4 splat8(uint32_t w) { return make_uint4(w, w, w, w); }
 
+// Load the C chunks of one row owned by this thread.
+template <int C, bool VEC, bool STREAM>
+__device__ __forceinline__ void load_row(uint4 (&dst)[C], const bf16* row, int64_t width) {
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+    dst[c] = load_chunk<VEC, STREAM>(row, ((int64_t)c * kThreads + threadIdx.x) * 8, width);
+}
+
+// Persistent row loop: CTA b handles rows b, b + gridDim.x, ...; for narrow
+// rows (C <= 4) the next row's chunks are loaded into registers before the
+// current row is reduced, so each CTA keeps one row of loads in flight while
+// it computes. Wider rows already issue C >= 6 loads per thread per row.
+template <int C>
+struct Prefetch {
+  static constexpr bool kOn = C <= 4;
+  static constexpr int kN = kOn ? C : 1;
+};
+
 // --------------------------------------------------------------------- K1
 template <int C, bool VEC>
 __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const bf16* __restrict__ x,
                                                                   int64_t row_stride, int width,
                                                                   int8_t* __restrict__ q,
-                                                                  float* __restrict__ scales) {
+                                                                  float* __restrict__ scales,
+                                                                  int64_t rows) {
   __shared__ float red[kWarps];
-  const int64_t row = blockIdx.x;
-  const bf16* src = x + row * row_stride;
+  int64_t row = blockIdx.x;
+  if (row >= rows) return;
   uint4 raw[C];
-  uint32_t amax2 = 0u;
+  load_row<C, VEC, true>(raw, x + row * row_stride, width);
+  while (true) {
+    const int64_t next = row + gridDim.x;
+    uint4 nxt[Prefetch<C>::kN];
+    if (Prefetch<C>::kOn && next < rows)
+      load_row<Prefetch<C>::kN, VEC, true>(nxt, x + next * row_stride, width);
+    uint32_t amax2 = 0u;
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    raw[c] = load_chunk<VEC, true>(src, col, width);
-    amax2 = bamax8(amax2, raw[c]);
-  }
-  const float amax = block_max<kWarps>(bamax_final(amax2), red);
-  const float s = row_scale_from_absmax(amax);
-  const float inv = __frcp_rn(s);
-  int8_t* dst = q + row * (int64_t)width;
+    for (int c = 0; c < C; ++c) amax2 = bamax8(amax2, raw[c]);
+    const float amax = block_max<kWarps>(bamax_final(amax2), red);
+    const float s = row_scale_from_absmax(amax);
+    const float inv = __frcp_rn(s);
+    int8_t* dst = q + row * (int64_t)width;
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    store_q8<VEC>(dst, col, width, quant8(raw[c], s, inv));
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      store_q8<VEC>(dst, col, width, quant8(raw[c], s, inv));
+    }
+    if (threadIdx.x == 0) scales[row] = s;
+    if (next >= rows) break;
+    if (Prefetch<C>::kOn) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) raw[c] = nxt[Prefetch<C>::kOn ? c : 0];
+    } else {
+      load_row<C, VEC, true>(raw, x + next * row_stride, width);
+    }
+    row = next;
   }
-  if (threadIdx.x == 0) scales[row] = s;
 }
 
 // --------------------------------------------------------------- K3/K4/K8
@@ -115,6 +147,7 @@ struct RmsArgs {
   int8_t* q;
   float* scales;
   bf16* out;
+  int64_t rows;
 };
 
 // Resolve the adaLN table row of flattened row `row`; null if the table is
@@ -133,36 +166,25 @@ __device__ __forceinline__ const bf16* table_row_ptr(const bf16* table, int64_t 
 }
 
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
-__global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
-  __shared__ float red[kWarps];
-  const int64_t row = blockIdx.x;
+__device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4 (&v)[C],
+                                            const uint4 (&d)[C], float* red) {
   const int hidden = a.hidden;
   bool bad;
   const bf16* trow = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence,
                                    row, bad);
   if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
   const bool have_table = trow != nullptr;
-  const bf16* src = a.x + row * (int64_t)hidden;
-
-  uint4 v[C];
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    v[c] = load_chunk<VEC, true>(src, col, hidden);
-  }
 
   if (RESID) {
     // v = bf16(x + bf16(gate * update))   (model/kernels.py:101-105)
-    const bf16* upd = a.update + row * (int64_t)hidden;
     const uint4 gate_default = splat8(a.table == nullptr ? kBf2One : 0u);
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      const uint4 d = load_chunk<VEC, true>(upd, col, hidden);
       const uint4 gt = have_table
                            ? load_chunk<VEC, false>(trow + (int64_t)a.gate_slot * hidden, col, hidden)
                            : gate_default;
-      v[c] = badd8(v[c], bmul8(gt, d));
+      v[c] = badd8(v[c], bmul8(gt, d[c]));
       store_chunk<VEC>(a.residual_out + row * (int64_t)hidden, col, hidden, v[c]);
     }
   }
@@ -232,34 +254,88 @@ __global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
   }
 }
 
+template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
+__global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
+  __shared__ float red[kWarps];
+  constexpr bool kPre = Prefetch<C>::kOn;
+  constexpr int kN = Prefetch<C>::kN;
+  constexpr int kD = RESID ? C : 1;
+  int64_t row = blockIdx.x;
+  if (row >= a.rows) return;
+  uint4 v[C], d[kD];
+  load_row<C, VEC, true>(v, a.x + row * (int64_t)a.hidden, a.hidden);
+  if (RESID) load_row<kD, VEC, true>(d, a.update + row * (int64_t)a.hidden, a.hidden);
+  while (true) {
+    const int64_t next = row + gridDim.x;
+    uint4 nv[kN], nd[RESID ? kN : 1];
+    if (kPre && next < a.rows) {
+      load_row<kN, VEC, true>(nv, a.x + next * (int64_t)a.hidden, a.hidden);
+      if (RESID) load_row<RESID ? kN : 1, VEC, true>(nd, a.update + next * (int64_t)a.hidden, a.hidden);
+    }
+    uint4 dd[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) dd[c] = d[RESID ? c : 0];
+    rms_mod_row<C, VEC, RESID, MOD, QUANT>(a, row, v, dd, red);
+    if (next >= a.rows) break;
+    if (kPre) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        v[c] = nv[kPre ? c : 0];
+        if (RESID) d[RESID ? c : 0] = nd[(RESID && kPre) ? c : 0];
+      }
+    } else {
+      load_row<C, VEC, true>(v, a.x + next * (int64_t)a.hidden, a.hidden);
+      if (RESID) load_row<kD, VEC, true>(d, a.update + next * (int64_t)a.hidden, a.hidden);
+    }
+    row = next;
+  }
+}
+
 // --------------------------------------------------------------------- K5
 template <int C, bool VEC>
 __global__ void __launch_bounds__(kThreads) gated_residual_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ y, const bf16* __restrict__ table,
     int64_t table_rows, int64_t table_width, const int64_t* __restrict__ indices,
-    int64_t sequence, int hidden, int gate_slot, bf16* __restrict__ out) {
-  const int64_t row = blockIdx.x;
-  bool bad;
-  const bf16* trow = table_row_ptr(table, table_rows, table_width, indices, sequence, row, bad);
-  if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
+    int64_t sequence, int hidden, int gate_slot, bf16* __restrict__ out, int64_t rows) {
+  constexpr bool kPre = Prefetch<C>::kOn;
+  constexpr int kN = Prefetch<C>::kN;
   const uint4 gate_default = splat8(table == nullptr ? kBf2One : 0u);
-  const bf16* xr = x + row * (int64_t)hidden;
-  const bf16* yr = y + row * (int64_t)hidden;
+  int64_t row = blockIdx.x;
+  if (row >= rows) return;
   uint4 xv[C], yv[C];
+  load_row<C, VEC, true>(xv, x + row * (int64_t)hidden, hidden);
+  load_row<C, VEC, true>(yv, y + row * (int64_t)hidden, hidden);
+  while (true) {
+    const int64_t next = row + gridDim.x;
+    uint4 nx[kN], ny[kN];
+    if (kPre && next < rows) {
+      load_row<kN, VEC, true>(nx, x + next * (int64_t)hidden, hidden);
+      load_row<kN, VEC, true>(ny, y + next * (int64_t)hidden, hidden);
+    }
+    bool bad;
+    const bf16* trow = table_row_ptr(table, table_rows, table_width, indices, sequence, row, bad);
+    if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    xv[c] = load_chunk<VEC, true>(xr, col, hidden);
-    yv[c] = load_chunk<VEC, true>(yr, col, hidden);
-  }
+    for (int c = 0; c < C; ++c) {
+      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+      const uint4 gt = trow != nullptr
+                           ? load_chunk<VEC, false>(trow + (int64_t)gate_slot * hidden, col, hidden)
+                           : gate_default;
+      // out = bf16(x + bf16(gate * y))   (model/kernels.py:146-153)
+      store_chunk<VEC>(out + row * (int64_t)hidden, col, hidden, badd8(xv[c], bmul8(gt, yv[c])));
+    }
+    if (next >= rows) break;
+    if (kPre) {
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    const uint4 gt = trow != nullptr
-                         ? load_chunk<VEC, false>(trow + (int64_t)gate_slot * hidden, col, hidden)
-                         : gate_default;
-    // out = bf16(x + bf16(gate * y))   (model/kernels.py:146-153)
-    store_chunk<VEC>(out + row * (int64_t)hidden, col, hidden, badd8(xv[c], bmul8(gt, yv[c])));
+      for (int c = 0; c < C; ++c) {
+        xv[c] = nx[kPre ? c : 0];
+        yv[c] = ny[kPre ? c : 0];
+      }
+    } else {
+      load_row<C, VEC, true>(xv, x + next * (int64_t)hidden, hidden);
+      load_row<C, VEC, true>(yv, y + next * (int64_t)hidden, hidden);
+    }
+    row = next;
   }
 }
 
@@ -273,40 +349,42 @@ template <int C, bool VEC, bool QUANT>
 __global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict__ projected,
                                                           int inner, bf16* __restrict__ out,
                                                           int8_t* __restrict__ q,
-                                                          float* __restrict__ scales) {
+                                                          float* __restrict__ scales,
+                                                          int64_t rows) {
   __shared__ float red[kWarps];
-  const int64_t row = blockIdx.x;
-  const bf16* value = projected + row * 2 * (int64_t)inner;
-  const bf16* gate = value + inner;
-  uint4 v[C];
-  uint32_t amax2 = 0u;
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-    float gf[8];
-    unpack8(load_chunk<VEC, true>(gate, col, inner), gf);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) gf[e] = silu(gf[e]);
-    // bf16(value * bf16(silu(gate)))
-    v[c] = bmul8(load_chunk<VEC, true>(value, col, inner), pack8(gf));
-    if (QUANT) amax2 = bamax8(amax2, v[c]);
-  }
-  if (QUANT) {
-    const float amax = block_max<kWarps>(bamax_final(amax2), red);
-    const float s = row_scale_from_absmax(amax);
-    const float inv = __frcp_rn(s);
-    int8_t* dst = q + row * (int64_t)inner;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const bf16* value = projected + row * 2 * (int64_t)inner;
+    const bf16* gate = value + inner;
+    uint4 v[C];
+    uint32_t amax2 = 0u;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      store_q8<VEC>(dst, col, inner, quant8(v[c], s, inv));
+      float gf[8];
+      unpack8(load_chunk<VEC, true>(gate, col, inner), gf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gf[e] = silu(gf[e]);
+      // bf16(value * bf16(silu(gate)))
+      v[c] = bmul8(load_chunk<VEC, true>(value, col, inner), pack8(gf));
+      if (QUANT) amax2 = bamax8(amax2, v[c]);
     }
-    if (threadIdx.x == 0) scales[row] = s;
-  } else {
+    if (QUANT) {
+      const float amax = block_max<kWarps>(bamax_final(amax2), red);
+      const float s = row_scale_from_absmax(amax);
+      const float inv = __frcp_rn(s);
+      int8_t* dst = q + row * (int64_t)inner;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      store_chunk<VEC>(out + row * (int64_t)inner, col, inner, v[c]);
+      for (int c = 0; c < C; ++c) {
+        const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+        store_q8<VEC>(dst, col, inner, quant8(v[c], s, inv));
+      }
+      if (threadIdx.x == 0) scales[row] = s;
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+        store_chunk<VEC>(out + row * (int64_t)inner, col, inner, v[c]);
+      }
     }
   }
 }
@@ -372,6 +450,31 @@ int pick_chunks(int64_t width) {
 
 constexpr int64_t kMaxRows = 0x7fffffff;
 
+// Grid of a persistent row kernel: every CTA that fits at once on the GPU
+// (occupancy of this instantiation x SM count), capped by the row count.
+template <typename Kernel>
+unsigned persistent_grid(Kernel kernel, int64_t rows, bool persistent = true) {
+  if (!persistent) return (unsigned)rows;  // one row per CTA
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> per_sm;
+  int n = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = per_sm.find(reinterpret_cast<const void*>(kernel));
+    if (it != per_sm.end()) {
+      n = it->second;
+    } else {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, 0) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 1;
+      }
+      per_sm.emplace(reinterpret_cast<const void*>(kernel), n);
+    }
+  }
+  const int64_t g = (int64_t)n * sm_count();
+  return (unsigned)(rows < g ? rows : g);
+}
+
 }  // namespace
 
 int read_status_elementwise(unsigned int* bits, int clear) {
@@ -409,9 +512,9 @@ extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int6
   const bf16* xp = static_cast<const bf16*>(x);
   LR_CHUNK_DISPATCH(C, {
     if (vec)
-      lr::quantize_rows_kernel<kC, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales);
+      lr::quantize_rows_kernel<kC, true><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows);
     else
-      lr::quantize_rows_kernel<kC, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales);
+      lr::quantize_rows_kernel<kC, false><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows);
   });
   return lr::launch_status("quantize_rows");
 }
@@ -464,7 +567,8 @@ static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, 
                       cudaStream_t s) {
   const int C = pick_chunks(a.hidden);
   if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln: hidden %d > 32768", a.hidden);
-#define LR_RMS(V, R, M, Q) lr::rms_mod_kernel<kC, V, R, M, Q><<<(unsigned)rows, lr::kThreads, 0, s>>>(a)
+#define LR_RMS(V, R, M, Q) \
+  lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(a)
 #define LR_RMS_Q(V, R, M)  \
   if (quant) LR_RMS(V, R, M, true); else LR_RMS(V, R, M, false)
 #define LR_RMS_M(V, R)     \
@@ -505,6 +609,7 @@ extern "C" int lr_rms_adaln(const void* x, const void* norm_weight, float eps, c
   a.shift_slot = shift_slot;
   a.scale_slot = scale_slot;
   a.out = static_cast<bf16*>(out);
+  a.rows = rows;
   const bool vec = vec_ok(hidden, {x, norm_weight, table, out}) && table_width % 8 == 0;
   return rms_launch(a, rows, false, table != nullptr, false, vec, static_cast<cudaStream_t>(stream));
 }
@@ -541,6 +646,7 @@ extern "C" int lr_rms_adaln_quant_int8(const void* x, const void* norm_weight, f
   a.residual_out = static_cast<bf16*>(residual_out);
   a.q = q;
   a.scales = scales;
+  a.rows = rows;
   const bool vec = vec_ok(hidden, {x, norm_weight, table, update, residual_out}) &&
                    (table == nullptr || table_width % 8 == 0) && lr::aligned(q, 8);
   return rms_launch(a, rows, update != nullptr, table != nullptr, true, vec,
@@ -567,11 +673,11 @@ extern "C" int lr_gated_residual(const void* x, const void* y, const void* table
   bf16* op = static_cast<bf16*>(out);
   LR_CHUNK_DISPATCH(C, {
     if (vec)
-      lr::gated_residual_kernel<kC, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(
-          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op);
+      lr::gated_residual_kernel<kC, true><<<lr::persistent_grid(lr::gated_residual_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(
+          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op, rows);
     else
-      lr::gated_residual_kernel<kC, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(
-          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op);
+      lr::gated_residual_kernel<kC, false><<<lr::persistent_grid(lr::gated_residual_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(
+          xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op, rows);
   });
   return lr::launch_status("gated_residual");
 }
@@ -591,11 +697,11 @@ static int swiglu_common(const char* who, const void* projected, int64_t rows, i
   bf16* o = static_cast<bf16*>(out);
   LR_CHUNK_DISPATCH(C, {
     if (vec) {
-      if (quant) lr::swiglu_kernel<kC, true, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
-      else lr::swiglu_kernel<kC, true, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+      if (quant) lr::swiglu_kernel<kC, true, true><<<lr::persistent_grid(lr::swiglu_kernel<kC, true, true>, rows, false), lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales, rows);
+      else lr::swiglu_kernel<kC, true, false><<<lr::persistent_grid(lr::swiglu_kernel<kC, true, false>, rows, false), lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales, rows);
     } else {
-      if (quant) lr::swiglu_kernel<kC, false, true><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
-      else lr::swiglu_kernel<kC, false, false><<<(unsigned)rows, lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales);
+      if (quant) lr::swiglu_kernel<kC, false, true><<<lr::persistent_grid(lr::swiglu_kernel<kC, false, true>, rows, false), lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales, rows);
+      else lr::swiglu_kernel<kC, false, false><<<lr::persistent_grid(lr::swiglu_kernel<kC, false, false>, rows, false), lr::kThreads, 0, s>>>(p, (int)inner, o, q, scales, rows);
     }
   });
   return lr::launch_status(who);

@@ -24,6 +24,17 @@
 #include "lr_common.cuh"
 #include "lr_host.h"
 
+// Compile-time tuning knobs of the pair kernel (defaults are the measured best).
+#ifndef LR_GEMM_STAGES2
+#define LR_GEMM_STAGES2 6
+#endif
+#ifndef LR_GEMM_L2_HINTS  // 0: default policy; 1: A panel evict-last; 2: also B evict-first
+#define LR_GEMM_L2_HINTS 0
+#endif
+#ifndef LR_GEMM_STREAM_STORES  // 1: evict-first (st.global.cs) output stores
+#define LR_GEMM_STREAM_STORES 0
+#endif
+
 namespace lr {
 
 static __device__ unsigned int g_gemm_status = 0;
@@ -269,12 +280,29 @@ __device__ __forceinline__ bool wait_bounded_cluster(uint32_t bar, uint32_t pari
 // mbarrier of either CTA of the pair (`bar` is a shared::cluster address).
 // No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int32_t x, int32_t y) {
+                                                 int32_t x, int32_t y, uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+// L2 eviction policies for the operand streams (LR_GEMM_L2_HINTS): the A panel
+// of a raster group is re-read for every N block.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 // Instruction descriptor of the pair MMA: M = 256 (128 rows per CTA), N = 256.
 constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -357,7 +385,10 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
                                 : make_uint4(gd, gd, gd, gd);
       y = badd8(x, bmul8(g, y));
     }
-    dst[q] = y;
+    if (LR_GEMM_STREAM_STORES)
+      __stcs(dst + q, y);  // evict-first output stores
+    else
+      dst[q] = y;
   }
 }
 
@@ -619,8 +650,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // rows of A and 128 rows (one N half) of B per 128-byte K step, the leader
 // (cluster rank 0) issues tcgen05.mma.cta_group::2 (M=256, N=256), and each CTA
 // drains its own 128-row accumulator from its TMEM. Per CTA a stage is 32 KB,
-// so six stages fit where the single-CTA kernel holds four.
-constexpr int STAGES2 = 6;
+// so six stages (192 KB) fit where the single-CTA kernel holds four.
+constexpr int STAGES2 = LR_GEMM_STAGES2;
 constexpr int A2_STAGE = 128 * BK;
 constexpr int B2_STAGE = 128 * BK;
 constexpr size_t SMEM2_BYTES = 1024 + (size_t)STAGES2 * (A2_STAGE + B2_STAGE) + BAR_BYTES;
@@ -686,6 +717,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------ TMA producer (both CTAs)
+      const uint64_t pol_a = LR_GEMM_L2_HINTS >= 1 ? l2_policy_evict_last() : l2_policy_evict_normal();
+      const uint64_t pol_b = LR_GEMM_L2_HINTS >= 2 ? l2_policy_evict_first() : l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
@@ -701,9 +734,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if (leader) mbar_expect_tx(fb, 2 * (A2_STAGE + B2_STAGE));
           const uint32_t fb_leader = map_to_rank(fb, 0);
           tma_load_2d_pair(smem_u32(sa + stage * A2_STAGE), &map_a, fb_leader, kb * BK,
-                           mb * 256 + (int)rank * 128);
+                           mb * 256 + (int)rank * 128, pol_a);
           tma_load_2d_pair(smem_u32(sb + stage * B2_STAGE), &map_b, fb_leader, kb * BK,
-                           nb * BN + (int)rank * 128);
+                           nb * BN + (int)rank * 128, pol_b);
           issued_any = true;
           if (++stage == STAGES2) {
             stage = 0;
