@@ -131,8 +131,9 @@ int lr_swiglu_quant_int8(const void* projected, int64_t rows, int64_t inner, int
  * `resid` (bf16 [M, N], row stride ldr; may alias `out` only if ldr == ldo)
  * and the gate table[indices[m % sequence], gate_slot*N + n]; `table` may be
  * NULL for gate = 1 (plain residual add). Unused residual arguments may be 0/NULL.
- * The tensor-core path (tcgen05, TMA) needs b_stride_k == 1, K % 16 == 0,
- * lda % 16 == 0, b_stride_n % 16 == 0 and 16-byte aligned a/b; other layouts
+ * The tensor-core path (tcgen05, TMA) needs b_stride_k == 1, lda % 16 == 0,
+ * b_stride_n % 16 == 0, 16-byte aligned a/b/out and N, ldo (and ldr) multiples
+ * of 8; other layouts
  * run a CUDA-core kernel with identical results. */
 int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
                  int64_t b_stride_n, int64_t M, int64_t N, int64_t K, const float* row_scale,
@@ -140,6 +141,27 @@ int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride
                  int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
                  const int64_t* indices, int64_t sequence, int gate_slot, void* out, int64_t ldo,
                  void* stream);
+
+/* Bytes of int32 workspace lr_int8_gemm_ws uses for this shape (slices x M x N
+ * int32), or 0 when the shape has enough output tiles to fill the GPU without
+ * splitting K. */
+int64_t lr_int8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* lr_int8_gemm with a caller-provided device workspace (no counterpart in the
+ * reference, which has no split-K). For shapes whose output tiles cannot fill
+ * the GPU (small M), K is split across CTA pairs: every K slice stores its
+ * partial int32 accumulators into its own M x N plane of the workspace, and a
+ * second kernel adds the planes in slice order (exact integer adds) and applies
+ * the epilogue. Results are identical to lr_int8_gemm. With workspace == NULL, or
+ * workspace_bytes < lr_int8_gemm_workspace_bytes(M, N, K), or a shape that
+ * needs no split, it behaves exactly like lr_int8_gemm. Calls sharing one
+ * workspace must be ordered on one stream. */
+int lr_int8_gemm_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                    int64_t b_stride_n, int64_t M, int64_t N, int64_t K, const float* row_scale,
+                    const float* col_scale, const void* bias, int epilogue, const void* resid,
+                    int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
+                    const int64_t* indices, int64_t sequence, int gate_slot, void* out,
+                    int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Raw int32 accumulators of the same GEMM (exactness checks of the integer path):
  *   acc[m,n] = sum_k a[m,k] * b[k,n], acc row stride N. */

@@ -44,6 +44,9 @@ SIGNATURES = {
     "lr_swiglu_quant_int8": ([_p, _i64, _i64, _p, _p, _p], _i32),
     "lr_int8_gemm": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
                       _i64, _i64, _p, _i64, _i32, _p, _i64, _p], _i32),
+    "lr_int8_gemm_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "lr_int8_gemm_ws": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
+                         _i64, _i64, _p, _i64, _i32, _p, _i64, _p, _i64, _p], _i32),
     "lr_int8_gemm_s32": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p], _i32),
 }
 
@@ -57,7 +60,7 @@ class LibraryError(RuntimeError):
 def header_symbols() -> list[str]:
     """Names of the entry points declared in include/lr_w8a8.h."""
     text = HEADER.read_text()
-    return re.findall(r"^(?:int|const char\*)\s+(lr_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^(?:int|int64_t|const char\*)\s+(lr_\w+)\s*\(", text, flags=re.M)
 
 
 def load(path: Path | None = None) -> ctypes.CDLL:

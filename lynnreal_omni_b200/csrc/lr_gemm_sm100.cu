@@ -58,7 +58,10 @@ constexpr int BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * (A_STAGE + B_STAGE) + BAR_BYTES;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
-enum Epi : int { kNone = 0, kGelu = 1, kGated = 2, kS32 = 3 };
+// kS32: store raw int32 accumulators ([M, N], row stride N); kS32Part: store a
+// K slice's partial accumulators into its own [M, N] plane of the split-K
+// workspace (plane = work item's slice).
+enum Epi : int { kNone = 0, kGelu = 1, kGated = 2, kS32 = 3, kS32Part = 4 };
 
 struct EpiArgs {
   const float* row_scale;
@@ -402,10 +405,11 @@ __device__ __forceinline__ void store_chunk_tail(const EpiArgs& ep, const uint32
   for (int j = 0; j < 32; ++j) {
     const int col = col0 + j;
     if (col >= N) break;
-    if (EPI == kS32) {
+    if (EPI == kS32 || EPI == kS32Part) {
       ep.acc_out[row * (int64_t)N + col] = (int32_t)acc[j];
       continue;
     }
+
     float d = dequant((int32_t)acc[j], rs, ep.col_scale[col]);
     if (bias != nullptr) d = __fadd_rn(d, bf_bits(bias[col]));
     float x = 0.0f, g = 0.0f;
@@ -432,7 +436,7 @@ __device__ __forceinline__ void drain_accumulator(const EpiArgs& ep, int M, int 
   const bf16* gptr = nullptr;
   bool have_gate = false;
   if (row_ok) {
-    if (EPI != kS32) rs = ep.row_scale[row];
+    if (EPI != kS32 && EPI != kS32Part) rs = ep.row_scale[row];
     if (EPI == kGated && ep.table != nullptr) {
       bool bad;
       const bf16* g = gate_row(ep, row, bad);
@@ -460,7 +464,7 @@ __device__ __forceinline__ void drain_accumulator(const EpiArgs& ep, int M, int 
     }
     const int col0 = col_base + c * 32;
     if (!row_ok || col0 >= N) continue;
-    if (EPI == kS32) {
+    if (EPI == kS32 || EPI == kS32Part) {
       if (col0 + 32 <= N && (N % 4) == 0) {
         int4* dst = reinterpret_cast<int4*>(ep.acc_out + row * (int64_t)N + col0);
 #pragma unroll
@@ -660,7 +664,7 @@ template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b, int M, int N, int K, int group_m,
-                    const EpiArgs ep) {
+                    int splits, const EpiArgs ep) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -683,6 +687,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int kblocks = (K + BK - 1) / BK;
+  // Split-K: work item w covers tile w / splits and K blocks
+  // [(w % splits) * kper, min(+kper, kblocks)); the host picks `splits` so
+  // that no slice is empty. With splits == 1 a work item is a whole tile.
+  const int kper = (kblocks + splits - 1) / splits;
+  const int work = tiles * splits;
   const int cluster_id = blockIdx.x >> 1;
   const int clusters = gridDim.x >> 1;
 
@@ -722,10 +731,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
-      for (int t = cluster_id; t < tiles && ok; t += clusters) {
+      for (int w = cluster_id; w < work && ok; w += clusters) {
+        const int t = w / splits;
+        const int kb0 = (w - t * splits) * kper;
+        const int kb1 = min(kb0 + kper, kblocks);
         int mb, nb;
         tile_coords(t, num_m, num_n, group_m, mb, nb);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -759,7 +771,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = cluster_id; t < tiles && ok; t += clusters, ++local) {
+      for (int w = cluster_id; w < work && ok; w += clusters, ++local) {
+        const int t = w / splits;
+        const int kb0 = (w - t * splits) * kper;
+        const int kb1 = min(kb0 + kper, kblocks);
         const int acc = local & 1;
         const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
         if (!wait_bounded_cluster(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag)) {
@@ -768,7 +783,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag)) {
             ok = false;
             break;
@@ -779,7 +794,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / UK; ++kk)
             mma_i8_pair(d_tmem, sw128_desc(a0 + kk * UK), sw128_desc(b0 + kk * UK),
-                        (kb | kk) != 0 ? 1u : 0u);
+                        (kb != kb0 || kk != 0) ? 1u : 0u);
           mma_commit_pair(smem_u32(&empty[stage]), (uint16_t)0x3);
           if (++stage == STAGES2) {
             stage = 0;
@@ -799,7 +814,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // -------------------------------------------- epilogue warps (both CTAs)
     const int quad = warp & 3;
     int local = 0;
-    for (int t = cluster_id; t < tiles; t += clusters, ++local) {
+    for (int w = cluster_id; w < work; w += clusters, ++local) {
+      const int t = w / splits;
       const int acc = local & 1;
       const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
       int ok = 1;
@@ -810,7 +826,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int mb, nb;
       tile_coords(t, num_m, num_n, group_m, mb, nb);
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      drain_accumulator<EPI>(ep, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32 + lane,
+      EpiArgs epw = ep;
+      if (EPI == kS32Part) epw.acc_out = ep.acc_out + (int64_t)(w - t * splits) * M * N;
+      drain_accumulator<EPI>(epw, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32 + lane,
                              nb * BN, lane, smem_u32(&tempty[acc]), 0, true);
     }
   }
@@ -823,6 +841,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(TMEM_COLS)
                  : "memory");
+  }
+}
+
+// ------------------------------------------------------- split-K finishing
+// Dequantise the summed int32 split-K workspace [M, N] and apply the epilogue:
+// one CTA per row, each thread 32 consecutive columns per step (same epilogue
+// code as the tensor-core kernels, so the bits are the same).
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_epilogue_kernel(const int32_t* __restrict__ ws, int M,
+                                                              int N, int splits, const EpiArgs ep,
+                                                              int vec) {
+  const int64_t row = blockIdx.x;
+  const float rs = ep.row_scale[row];
+  const bf16* gptr = nullptr;
+  bool have_gate = false;
+  if (EPI == kGated && ep.table != nullptr) {
+    bool bad;
+    const bf16* g = gate_row(ep, row, bad);
+    if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+    if (g != nullptr) {
+      gptr = g + (int64_t)ep.gate_slot * N;
+      have_gate = true;
+    }
+  }
+  const int64_t plane = (int64_t)M * N;
+  for (int col0 = threadIdx.x * 32; col0 < N; col0 += 256 * 32) {
+    uint32_t acc[32];
+    const int32_t* src = ws + row * (int64_t)N + col0;
+    const bool full = vec && col0 + 32 <= N;
+    // sum the K slices' partial accumulators, slice 0 first (exact int32 adds)
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        int4 sum = __ldcs(reinterpret_cast<const int4*>(src) + q);
+        for (int sp = 1; sp < splits; ++sp) {
+          const int4 v = __ldcs(reinterpret_cast<const int4*>(src + sp * plane) + q);
+          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+        }
+        acc[4 * q] = (uint32_t)sum.x;
+        acc[4 * q + 1] = (uint32_t)sum.y;
+        acc[4 * q + 2] = (uint32_t)sum.z;
+        acc[4 * q + 3] = (uint32_t)sum.w;
+      }
+      store_chunk_vec<EPI>(ep, acc, row, col0, rs, gptr, have_gate);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        int32_t sum = 0;
+        if (col0 + j < N)
+          for (int sp = 0; sp < splits; ++sp) sum += src[sp * plane + j];
+        acc[j] = (uint32_t)sum;
+      }
+      store_chunk_tail<EPI>(ep, acc, row, col0, N, rs, gptr, have_gate);
+    }
   }
 }
 
@@ -983,8 +1055,53 @@ int launch_tc2(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M
   const int pairs = sm_count() / 2;
   const int clusters = tiles < pairs ? tiles : pairs;
   gemm_tc2_kernel<EPI><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(
-      ma, mb, M, N, K, raster_group(256, num_m, K), ep);
+      ma, mb, M, N, K, raster_group(256, num_m, K), 1, ep);
   return launch_status("int8 gemm (tcgen05, CTA pair)");
+}
+
+// Number of K slices for a shape whose tiles cannot fill the GPU's CTA pairs
+// (1: no split). Each slice keeps at least 4 K blocks of 128.
+int splitk_slices(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
+  const int64_t pairs = sm_count() / 2;
+  const int64_t kblocks = (K + BK - 1) / BK;
+  if (tiles * 2 > pairs || kblocks < 8) return 1;
+  int64_t s = pairs / tiles;
+  if (s > kblocks / 4) s = kblocks / 4;
+  if (s > 16) s = 16;
+  if (s < 2) return 1;
+  const int64_t kper = (kblocks + s - 1) / s;
+  return (int)((kblocks + kper - 1) / kper);  // every slice non-empty
+}
+
+// Split-K on the CTA-pair kernel: each K slice stores its partial int32
+// accumulators into its own [M, N] plane of the workspace; the epilogue kernel
+// adds the planes in slice order and applies the epilogue.
+template <int EPI>
+int launch_tc2_splitk(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N,
+                      int K, int splits, int32_t* ws, const EpiArgs& ep, bool vec,
+                      cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 128);
+  if (st) return st;
+  st = make_map(&mb, b, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 128);
+  if (st) return st;
+  static bool done[64] = {};
+  st = configure_smem(gemm_tc2_kernel<kS32Part>, SMEM2_BYTES, done);
+  if (st) return st;
+  EpiArgs acc = {};
+  acc.acc_out = ws;
+  const int num_m = (M + 255) / 256;
+  const int work = num_m * ((N + BN - 1) / BN) * splits;
+  const int pairs = sm_count() / 2;
+  const int clusters = work < pairs ? work : pairs;
+  gemm_tc2_kernel<kS32Part><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(
+      ma, mb, M, N, K, raster_group(256, num_m, K), splits, acc);
+  st = launch_status("int8 gemm (tcgen05, CTA pair, split-K)");
+  if (st) return st;
+  splitk_epilogue_kernel<EPI><<<M, 256, 0, stream>>>(ws, M, N, splits, ep,
+                                                    (vec && N % 4 == 0 && aligned(ws, 16)) ? 1 : 0);
+  return launch_status("int8 gemm split-K epilogue");
 }
 
 template <int EPI>
@@ -998,9 +1115,18 @@ int launch_simt(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int6
 
 template <int EPI>
 int run(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int64_t bsn, int64_t M,
-        int64_t N, int64_t K, const EpiArgs& ep, bool out_vec_ok, cudaStream_t stream) {
+        int64_t N, int64_t K, const EpiArgs& ep, bool out_vec_ok, cudaStream_t stream,
+        int32_t* ws = nullptr, int64_t ws_bytes = 0) {
   const bool tc = bsk == 1 && K > 0 && lda % 16 == 0 && bsn % 16 == 0 && aligned(a, 16) &&
                   aligned(b, 16) && out_vec_ok;
+  if constexpr (EPI != kS32) {
+    if (tc && ws != nullptr) {
+      const int splits = splitk_slices(M, N, K);
+      if (splits > 1 && ws_bytes >= splits * M * N * (int64_t)sizeof(int32_t) && aligned(ws, 16))
+        return launch_tc2_splitk<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, splits, ws, ep,
+                                      out_vec_ok, stream);
+    }
+  }
   if (tc && M > BM) return launch_tc2<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream);
   if (tc) return launch_tc<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream);
   return launch_simt<EPI>(a, lda, b, bsk, bsn, (int)M, (int)N, (int)K, ep, stream);
@@ -1038,12 +1164,12 @@ int check_gemm_shape(const char* who, const int8_t* a, int64_t lda, const int8_t
 
 }  // namespace
 
-extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
-                            int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
-                            const float* row_scale, const float* col_scale, const void* bias,
-                            int epilogue, const void* resid, int64_t ldr, const void* table,
-                            int64_t table_rows, int64_t table_width, const int64_t* indices,
-                            int64_t sequence, int gate_slot, void* out, int64_t ldo, void* stream) {
+static int gemm_entry(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                      int64_t b_stride_n, int64_t M, int64_t N, int64_t K, const float* row_scale,
+                      const float* col_scale, const void* bias, int epilogue, const void* resid,
+                      int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
+                      const int64_t* indices, int64_t sequence, int gate_slot, void* out,
+                      int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace lr::gemm;
   int st = check_gemm_shape("int8_gemm", a, lda, b, b_stride_k, b_stride_n, M, N, K);
   if (st) return st;
@@ -1083,14 +1209,44 @@ extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64
           (table == nullptr || (lr::aligned(table, 16) && table_width % 8 == 0));
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* ws = static_cast<int32_t*>(workspace);
   switch (epilogue) {
     case LR_EPI_GELU_TANH:
-      return run<kGelu>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+      return run<kGelu>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
     case LR_EPI_GATED_RESIDUAL:
-      return run<kGated>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+      return run<kGated>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
     default:
-      return run<kNone>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s);
+      return run<kNone>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
   }
+}
+
+extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                            int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
+                            const float* row_scale, const float* col_scale, const void* bias,
+                            int epilogue, const void* resid, int64_t ldr, const void* table,
+                            int64_t table_rows, int64_t table_width, const int64_t* indices,
+                            int64_t sequence, int gate_slot, void* out, int64_t ldo, void* stream) {
+  return gemm_entry(a, lda, b, b_stride_k, b_stride_n, M, N, K, row_scale, col_scale, bias,
+                    epilogue, resid, ldr, table, table_rows, table_width, indices, sequence,
+                    gate_slot, out, ldo, nullptr, 0, stream);
+}
+
+extern "C" int64_t lr_int8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M >= (1ll << 31) || N >= (1ll << 31)) return 0;
+  const int splits = lr::gemm::splitk_slices(M, N, K);
+  return splits > 1 ? splits * M * N * (int64_t)sizeof(int32_t) : 0;
+}
+
+extern "C" int lr_int8_gemm_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                               int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
+                               const float* row_scale, const float* col_scale, const void* bias,
+                               int epilogue, const void* resid, int64_t ldr, const void* table,
+                               int64_t table_rows, int64_t table_width, const int64_t* indices,
+                               int64_t sequence, int gate_slot, void* out, int64_t ldo,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_entry(a, lda, b, b_stride_k, b_stride_n, M, N, K, row_scale, col_scale, bias,
+                    epilogue, resid, ldr, table, table_rows, table_width, indices, sequence,
+                    gate_slot, out, ldo, workspace, workspace_bytes, stream);
 }
 
 extern "C" int lr_int8_gemm_s32(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,

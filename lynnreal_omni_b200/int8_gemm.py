@@ -72,10 +72,15 @@ def _launch(a, b, row_scale, column_scale, bias, epilogue, residual=None, table=
             idx = indices.reshape(-1).to(torch.int64).contiguous()
             if idx.numel() < seq:
                 raise ValueError(f"expected at least {seq} adaLN indices, got {idx.numel()}")
-    check(_lib.load().lr_int8_gemm(
+    lib = _lib.load()
+    ws_bytes = lib.lr_int8_gemm_workspace_bytes(m, n, k)
+    # small-M shapes split K across the GPU: the int32 partial-sum workspace
+    # comes from torch's caching allocator (the library allocates nothing)
+    ws = torch.empty(ws_bytes // 4, device=a.device, dtype=torch.int32) if ws_bytes > 0 else None
+    check(lib.lr_int8_gemm_ws(
         ptr(a), a.stride(0), ptr(b), b.stride(0), b.stride(1), m, n, k, ptr(rs), ptr(cs), ptr(bb),
         epilogue, resid_ptr, ldr, ptr(tbl), trows, twidth, ptr(idx), seq, gate_slot, ptr(output),
-        output.stride(0), stream_of(a)), "int8_matmul")
+        output.stride(0), ptr(ws), ws_bytes, stream_of(a)), "int8_matmul")
     return output
 
 

@@ -17,14 +17,28 @@ from types import SimpleNamespace
 import torch
 
 
-def _time(fn, iters: int, warmup: int):
+def _time(fn, iters: int, warmup: int, graph: bool = False):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if graph:
+        # capture `iters` calls once and time one replay: device time without
+        # the host-side cost of issuing each call
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
+        reps = 1
+    else:
+        run = fn
+        reps = iters
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(iters):
-        fn()
+    for _ in range(reps):
+        run()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
@@ -40,13 +54,14 @@ def main(argv=None):
     p.add_argument("--epi", choices=["none", "gelu", "gated"], default="none")
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--graph", action="store_true", help="time a CUDA-graph replay of the launches")
     a = p.parse_args(argv)
 
     from . import kernels as K
     from .int8_gemm import int8_matmul, int8_matmul_gated_residual, int8_matmul_gelu
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    out = {"case": a.case}
+    out = {"case": a.case, "graph": a.graph}
     if a.case == "gemm":
         A = torch.randint(-127, 128, (a.m, a.k), device=dev, dtype=torch.int8, generator=g)
         B = torch.randint(-127, 128, (a.n, a.k), device=dev, dtype=torch.int8, generator=g).t()
@@ -62,7 +77,7 @@ def main(argv=None):
             fn = lambda: int8_matmul_gated_residual(A, B, rs, cs, bias, res, table, idx, 5)  # noqa: E731
         else:
             fn = lambda: int8_matmul(A, B, rs, cs, bias)  # noqa: E731
-        ms = _time(fn, a.iters, a.warmup)
+        ms = _time(fn, a.iters, a.warmup, a.graph)
         out.update(m=a.m, k=a.k, n=a.n, epi=a.epi, ms=ms, tops=2.0 * a.m * a.n * a.k / (ms / 1e3) / 1e12,
                    algorithmic_bytes=a.m * a.k + a.n * a.k + 2 * a.m * a.n + 4 * a.m + 6 * a.n)
     else:
@@ -80,7 +95,7 @@ def main(argv=None):
             fn, per_elem = (lambda: K._gated_residual(x, y, table, idx, 2)), 6
         else:
             fn, per_elem = (lambda: K.residual_rms_quant(x, y, norm, table, idx)), 7
-        ms = _time(fn, a.iters, a.warmup)
+        ms = _time(fn, a.iters, a.warmup, a.graph)
         nbytes = per_elem * a.m * a.d + 4 * a.m
         out.update(m=a.m, d=a.d, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
     print(json.dumps(out), flush=True)

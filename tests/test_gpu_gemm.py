@@ -210,3 +210,58 @@ def test_empty_rows():
     b = torch.zeros(64, 32, dtype=torch.int8, device=DEV)
     y = int8_matmul(a, b, torch.ones(0, 1, device=DEV), torch.ones(1, 32, device=DEV))
     assert y.shape == (0, 32)
+
+
+SPLITK = [(256, 6144, 6144), (32, 6144, 6144), (7, 24576, 6144), (64, 4096, 6144), (1, 6144, 2048),
+          (300, 2048, 1024)]
+
+
+@pytest.mark.parametrize("m,k,n", SPLITK)
+def test_split_k_small_m_exact(m, k, n):
+    """Small-M shapes split K across the GPU (int32 partial sums added into a
+    workspace); the result is bit-identical to the unsplit GEMM."""
+    assert _lib.load().lr_int8_gemm_workspace_bytes(m, n, k) % (m * n * 4) == 0
+    assert _lib.load().lr_int8_gemm_workspace_bytes(m, n, k) >= 2 * m * n * 4
+    a, b, rs, cs, bias = workloads.gemm_operands(m, k, n, seed=m * 3 + n, bias=True)
+    y = int8_matmul(a.to(DEV), b.to(DEV), rs.to(DEV), cs.to(DEV), bias.to(DEV))
+    ref = O.int8_matmul(a.numpy(), b.numpy(), rs.numpy(), cs.numpy(), O.to_numpy_f32(bias))
+    np.testing.assert_array_equal(bits(y), O.bf16_bits(ref))
+
+
+def test_split_k_gated_and_plain_path_agree():
+    m, k, n = 48, 6144, 6144
+    a, b, rs, cs, bias = workloads.gemm_operands(m, k, n, seed=77, bias=True)
+    gen = torch.Generator().manual_seed(77)
+    resid = torch.randn(1, m, n, generator=gen).to(torch.bfloat16)
+    table = (0.3 * torch.randn(2, 6 * n, generator=gen)).to(torch.bfloat16)
+    idx = torch.randint(0, 2, (m,), generator=gen)
+    args = [t.to(DEV) for t in (a, b, rs, cs, bias)]
+    split = int8_matmul_gated_residual(*args, resid.to(DEV), table.to(DEV), idx.to(DEV), 5)
+    ref = O.int8_matmul_gated_residual(a.numpy(), b.numpy(), rs.numpy(), cs.numpy(), O.to_numpy_f32(bias),
+                                       O.to_numpy_f32(resid).reshape(m, n), O.to_numpy_f32(table), idx.numpy(), 5)
+    np.testing.assert_array_equal(bits(split).reshape(m, n), O.bf16_bits(ref))
+    # the same call without a workspace (no split) gives the same bits
+    lib = _lib.load()
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    a_d, b_d, rs_d, cs_d, bias_d = args
+    r_d, t_d, i_d = resid.to(DEV).view(m, n), table.to(DEV), idx.to(DEV)
+    _lib.check(lib.lr_int8_gemm(a_d.data_ptr(), k, b_d.data_ptr(), 1, k, m, n, k, rs_d.data_ptr(), cs_d.data_ptr(),
+                                bias_d.data_ptr(), _lib.LR_EPI_GATED_RESIDUAL, r_d.data_ptr(), n, t_d.data_ptr(), 2,
+                                6 * n, i_d.data_ptr(), m, 5, out.data_ptr(), n,
+                                torch.cuda.current_stream().cuda_stream), "gemm")
+    assert torch.equal(out, split.view(m, n))
+
+
+def test_split_k_gelu_matches_unsplit_bits():
+    m, k, n = 40, 6144, 4096
+    a, b, rs, cs, bias = workloads.gemm_operands(m, k, n, seed=5, bias=True)
+    args = [t.to(DEV) for t in (a, b, rs, cs * 4, bias)]
+    split = int8_matmul_gelu(*args)
+    lib = _lib.load()
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    a_d, b_d, rs_d, cs_d, bias_d = args
+    _lib.check(lib.lr_int8_gemm(a_d.data_ptr(), k, b_d.data_ptr(), 1, k, m, n, k, rs_d.data_ptr(),
+                                cs_d.contiguous().data_ptr(), bias_d.data_ptr(), _lib.LR_EPI_GELU_TANH, None, 0,
+                                None, 0, 0, None, 1, 0, out.data_ptr(), n,
+                                torch.cuda.current_stream().cuda_stream), "gemm")
+    assert torch.equal(out, split)

@@ -39,6 +39,16 @@ def test_library_version_and_error_path_without_gpu():
         _lib.check(st, "int8_matmul")
 
 
+def test_workspace_query():
+    """Split-K needs an M*N int32 workspace only when the output tiles cannot
+    fill the GPU (small M); large shapes need none."""
+    lib = _lib.load()
+    assert lib.lr_int8_gemm_workspace_bytes(256, 6144, 6144) == 3 * 256 * 6144 * 4  # 3 K slices
+    assert lib.lr_int8_gemm_workspace_bytes(12240, 24576, 6144) == 0
+    assert lib.lr_int8_gemm_workspace_bytes(256, 6144, 512) == 0  # too little K to split
+    assert lib.lr_int8_gemm_workspace_bytes(0, 6144, 6144) == 0
+
+
 def test_empty_rows_are_a_no_op():
     lib = _lib.load()
     assert lib.lr_quantize_rows(None, 0, 64, 64, None, None, None) == _lib.LR_OK
