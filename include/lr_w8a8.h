@@ -163,6 +163,33 @@ int lr_int8_gemm_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_str
                     const int64_t* indices, int64_t sequence, int gate_slot, void* out,
                     int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Size of the fixed split-K scratch array behind lr_int8_gemm_noalloc. */
+#define LR_NOALLOC_SCRATCH_BYTES (16ll << 20)
+
+/* lr_int8_gemm for callers that cannot allocate device memory — a plugin or
+ * FFI host that only hands over the tensors it already owns, or a framework
+ * whose memory pool must not grow during a step. No counterpart in the
+ * reference. Same arguments and same results as lr_int8_gemm; where the shape
+ * is small enough in M to split K (lr_int8_gemm_workspace_bytes > 0), the
+ * split-K scratch is a fixed 16 MiB array compiled into this library, which
+ * every GPU that loads the library holds until the process exits. It calls no
+ * cudaMalloc or cudaFree and never allocates.
+ *   - A shape whose split-K scratch exceeds LR_NOALLOC_SCRATCH_BYTES is
+ *     rejected with LR_ERR_UNSUPPORTED (use lr_int8_gemm_ws with a workspace).
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents;
+ *     nothing in it needs to start at zero (each call writes every element it
+ *     later reads). Calls that overlap on the GPU (concurrent streams, or
+ *     several host threads) race on the array: order them on one stream. */
+int lr_int8_gemm_noalloc(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                         int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
+                         const float* row_scale, const float* col_scale, const void* bias,
+                         int epilogue, const void* resid, int64_t ldr, const void* table,
+                         int64_t table_rows, int64_t table_width, const int64_t* indices,
+                         int64_t sequence, int gate_slot, void* out, int64_t ldo, void* stream);
+
 /* Raw int32 accumulators of the same GEMM (exactness checks of the integer path):
  *   acc[m,n] = sum_k a[m,k] * b[k,n], acc row stride N. */
 int lr_int8_gemm_s32(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,

@@ -47,6 +47,8 @@ SIGNATURES = {
     "lr_int8_gemm_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "lr_int8_gemm_ws": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
                          _i64, _i64, _p, _i64, _i32, _p, _i64, _p, _i64, _p], _i32),
+    "lr_int8_gemm_noalloc": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
+                              _i64, _i64, _p, _i64, _i32, _p, _i64, _p], _i32),
     "lr_int8_gemm_s32": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p], _i32),
 }
 

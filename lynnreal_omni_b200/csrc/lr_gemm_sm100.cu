@@ -21,6 +21,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "lr_common.cuh"
 #include "lr_host.h"
 
@@ -1261,4 +1263,70 @@ extern "C" int lr_int8_gemm_s32(const int8_t* a, int64_t lda, const int8_t* b, i
   ep.acc_out = acc;
   return run<kS32>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, lr::aligned(acc, 16),
                    static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------- allocation-free GEMM
+// Some callers cannot allocate device memory at the point where they run the
+// GEMM: a host that hands this library only the tensors it already owns (a
+// plugin or FFI caller with no allocator, a framework whose memory pool is
+// frozen during a step). For them lr_int8_gemm_noalloc runs the same GEMM with
+// the split-K scratch taken from this fixed array instead of a caller
+// workspace. The array is LR_NOALLOC_SCRATCH_BYTES (16 MiB) and lives on every
+// GPU that loads the library until the process exits.
+static __device__ __align__(256) int32_t g_noalloc_scratch[LR_NOALLOC_SCRATCH_BYTES / sizeof(int32_t)];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// array's name only stands for the symbol, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return lr::launch_status("noalloc scratch: cudaGetDevice");
+  if (dev < 0 || dev >= 64)
+    return lr::set_error(LR_ERR_UNSUPPORTED, "noalloc scratch: device %d is out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return lr::set_error(LR_ERR_CUDA, "noalloc scratch: cudaGetSymbolAddress failed (%s)",
+                           cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return LR_OK;
+}
+
+}  // namespace
+
+extern "C" int lr_int8_gemm_noalloc(const int8_t* a, int64_t lda, const int8_t* b,
+                                    int64_t b_stride_k, int64_t b_stride_n, int64_t M, int64_t N,
+                                    int64_t K, const float* row_scale, const float* col_scale,
+                                    const void* bias, int epilogue, const void* resid, int64_t ldr,
+                                    const void* table, int64_t table_rows, int64_t table_width,
+                                    const int64_t* indices, int64_t sequence, int gate_slot,
+                                    void* out, int64_t ldo, void* stream) {
+  const int64_t need = lr_int8_gemm_workspace_bytes(M, N, K);  // 0: this shape runs unsplit
+  if (need > (int64_t)LR_NOALLOC_SCRATCH_BYTES)
+    return lr::set_error(LR_ERR_UNSUPPORTED,
+                         "int8_gemm_noalloc: M=%lld N=%lld K=%lld needs %lld bytes of split-K "
+                         "scratch, more than the %lld-byte static maximum; use lr_int8_gemm_ws "
+                         "with a caller-provided workspace",
+                         (long long)M, (long long)N, (long long)K, (long long)need,
+                         (long long)LR_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = noalloc_scratch(&scratch);
+    if (st) return st;
+  }
+  return gemm_entry(a, lda, b, b_stride_k, b_stride_n, M, N, K, row_scale, col_scale, bias,
+                    epilogue, resid, ldr, table, table_rows, table_width, indices, sequence,
+                    gate_slot, out, ldo, scratch, need > 0 ? (int64_t)LR_NOALLOC_SCRATCH_BYTES : 0,
+                    stream);
 }
