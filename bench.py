@@ -47,9 +47,10 @@ def parse_args():
     p.add_argument("--cpu-sample-rows", type=int, default=512)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=["block", "stack"], default="block",
+    p.add_argument("--workload", choices=["block", "stack", "sweep"], default="block",
                    help="block: config 2 per GPU (weak scaling); stack: config 4, 42 blocks x 3 denoiser "
-                        "steps on 64512 tokens sharded over the GPUs with a final all-gather")
+                        "steps on 64512 tokens sharded over the GPUs with a final all-gather; sweep: "
+                        "config 3 GEMM shapes, row-sharded, TOP/s per shape beside cuBLASLt")
     p.add_argument("--layers", type=int, default=42)
     p.add_argument("--stack-tokens", type=int, default=64512)
     return p.parse_args()
@@ -507,6 +508,83 @@ def run_stack(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_sweep(args, rank, world, local):
+    """Config 3: INT8 GEMM sweep M x (K, N), each shape's rows sharded over the
+    ranks. Per shape: our GEMM (bf16 dequant epilogue) and cuBLASLt torch._int_mm
+    (int32 out, no epilogue) on the same operands, each timed as a CUDA-graph
+    replay of `steps` launches (device time, no host issue cost), max over ranks."""
+    import torch.distributed as dist
+    from lynnreal_omni_b200 import _lib, workloads as W
+    from lynnreal_omni_b200.int8_gemm import int8_matmul
+    from lynnreal_omni_b200.parallel import shard_bounds
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    _lib.load()
+
+    def graph_ms(fn, reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        g.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([t0.elapsed_time(t1) / reps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        return t.item()
+
+    peaks = measured_peaks()
+    peak = 2.0 * (peaks.get("bf16_tflops") or FALLBACK_BF16_BURST_TFLOPS)
+    rows = []
+    for m_total in W.SWEEP_M:
+        start, stop = shard_bounds(m_total, world, rank)
+        m = stop - start
+        for k, n in W.SWEEP_KN:
+            gen = W.generator(1000 + m_total + k + n + rank, dev)
+            a = torch.randint(-127, 128, (m, k), generator=gen, device=dev, dtype=torch.int8)
+            b = torch.randint(-127, 128, (n, k), generator=gen, device=dev, dtype=torch.int8).t()
+            rs = torch.rand(m, 1, generator=gen, device=dev) / 127
+            cs = torch.rand(1, n, generator=gen, device=dev) / 127
+            reps = max(3, min(args.steps, int(2e12 // max(1, 2 * m * n * k)) + 3))
+            ours = graph_ms(lambda: int8_matmul(a, b, rs, cs), reps)
+            a_pad = a if m >= 32 and m % 8 == 0 else torch.nn.functional.pad(a, (0, 0, 0, max(32, -(-m // 8) * 8) - m))
+            cublas = graph_ms(lambda: torch._int_mm(a_pad, b), reps)
+            ops = 2.0 * m_total * n * k
+            rows.append({"m": m_total, "k": k, "n": n, "m_per_gpu": m, "ms": ours,
+                         "tops": ops / (ours / 1e3) / 1e12, "frac_of_peak": ops / (ours / 1e3) / 1e12 / peak,
+                         "cublaslt_int_mm_ms": cublas, "cublaslt_tops": ops / (cublas / 1e3) / 1e12,
+                         "split_k": _lib.load().lr_int8_gemm_workspace_bytes(m, n, k) > 0})
+            del a, b, rs, cs, a_pad
+            torch.cuda.empty_cache()
+    if rank == 0:
+        total_ops = sum(2.0 * r["m"] * r["n"] * r["k"] for r in rows)
+        total_ms = sum(r["ms"] for r in rows)
+        line = {"metric": METRIC, "workload": "config3 GEMM sweep",
+                "value": total_ops / (total_ms / 1e3) / 1e12, "unit": "TOP/s (int8, all shapes)",
+                "n_gpus": world, "steps": args.steps, "higher_is_better": True, "scaling": "strong",
+                "dtype": "int8", "data": "synthetic (seeded)", "peak": peak,
+                "peak_source": "of measured: 2 x bf16_tflops burst (MEASURED_PEAKS.json)",
+                "timing": "CUDA-graph replay per shape, device time, max over ranks",
+                "shapes": rows}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
@@ -516,6 +594,8 @@ def main():
         return
     if args.workload == "stack":
         run_stack(args, rank, world, local)
+    elif args.workload == "sweep":
+        run_sweep(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

@@ -20,6 +20,18 @@ static __device__ unsigned int g_device_status = 0;
 
 __device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_device_status, bits); }
 
+}  // namespace lr
+
+#include "lr_rows.cuh"
+
+namespace lr {
+using rows::load_chunk;
+using rows::store_chunk;
+using rows::store_q8;
+using rows::splat8;
+using rows::RmsArgs;
+using rows::table_row_ptr;
+
 namespace {
 
 constexpr int kThreads = 256;
@@ -27,50 +39,6 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kSpan = kThreads * 8;  // columns covered by one chunk sweep
 
 using bf16 = __nv_bfloat16;
-
-// Load the 8-column chunk starting at `col` of a row (zeros past `width`).
-// VEC: the chunk is 16-byte aligned and either fully inside or fully outside.
-template <bool VEC, bool STREAM>
-__device__ __forceinline__ uint4 load_chunk(const bf16* row, int64_t col, int64_t width) {
-  if (VEC) {
-    if (col < width) return STREAM ? ld_stream(row + col) : ld_keep(row + col);
-    return make_uint4(0u, 0u, 0u, 0u);
-  } else {
-    const uint16_t* p = reinterpret_cast<const uint16_t*>(row);
-    uint32_t h[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = (col + e < width) ? p[col + e] : 0u;
-    return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                      h[6] | (h[7] << 16));
-  }
-}
-
-template <bool VEC>
-__device__ __forceinline__ void store_chunk(bf16* row, int64_t col, int64_t width, const uint4& v) {
-  if (VEC) {
-    if (col < width) *reinterpret_cast<uint4*>(row + col) = v;
-  } else {
-    uint16_t* p = reinterpret_cast<uint16_t*>(row);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (col + e < width) p[col + e] = (uint16_t)(w[e >> 1] >> ((e & 1) * 16));
-  }
-}
-
-// Store eight int8 values (packed in a uint2) at q[col..col+7].
-template <bool VEC>
-__device__ __forceinline__ void store_q8(int8_t* q, int64_t col, int64_t width, const uint2& w) {
-  if (VEC) {
-    if (col < width) *reinterpret_cast<uint2*>(q + col) = w;
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (col + e < width) q[col + e] = (int8_t)((e < 4 ? w.x : w.y) >> (8 * (e & 3)));
-  }
-}
-
-__device__ __forceinline__ uint4 splat8(uint32_t w) { return make_uint4(w, w, w, w); }
 
 // Load the C chunks of one row owned by this thread.
 template <int C, bool VEC, bool STREAM>
@@ -132,39 +100,6 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const bf16* __r
 }
 
 // --------------------------------------------------------------- K3/K4/K8
-struct RmsArgs {
-  const bf16* x;
-  const bf16* update;  // K8 residual branch (may be null)
-  const bf16* weight;
-  float eps;
-  const bf16* table;  // may be null: no modulation, gate 1
-  int64_t table_rows, table_width;
-  const int64_t* indices;
-  int64_t sequence;
-  int hidden;
-  int shift_slot, scale_slot, gate_slot;
-  bf16* residual_out;
-  int8_t* q;
-  float* scales;
-  bf16* out;
-  int64_t rows;
-};
-
-// Resolve the adaLN table row of flattened row `row`; null if the table is
-// absent, or (with the status bit raised) if the index is out of range.
-__device__ __forceinline__ const bf16* table_row_ptr(const bf16* table, int64_t table_rows,
-                                                     int64_t table_width, const int64_t* indices,
-                                                     int64_t sequence, int64_t row, bool& bad) {
-  bad = false;
-  if (table == nullptr) return nullptr;
-  const int64_t tr = indices[row % sequence];
-  if (tr < 0 || tr >= table_rows) {
-    bad = true;
-    return nullptr;
-  }
-  return table + tr * table_width;
-}
-
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
 __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4 (&v)[C],
                                             const uint4 (&d)[C], float* red) {
@@ -288,6 +223,170 @@ __global__ void __launch_bounds__(kThreads) rms_mod_kernel(const RmsArgs a) {
       if (RESID) load_row<kD, VEC, true>(d, a.update + next * (int64_t)a.hidden, a.hidden);
     }
     row = next;
+  }
+}
+
+// Two rows per CTA: both rows' partial sums (and then absmaxes) go through one
+// block reduction, halving the barriers per row and giving each thread two
+// independent rows of work between them. Each row's reduction tree is exactly
+// the single-row tree (block_sum2 / block_max2 reduce the two components
+// separately in the same order), so results are identical to rms_mod_kernel.
+template <int NWARPS>
+__device__ __forceinline__ float2 block_sum2(float2 v, float2* scratch) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    v.x = __fadd_rn(v.x, __shfl_xor_sync(0xffffffffu, v.x, off));
+    v.y = __fadd_rn(v.y, __shfl_xor_sync(0xffffffffu, v.y, off));
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float2 s[NWARPS];
+#pragma unroll
+  for (int w = 0; w < NWARPS; ++w) s[w] = scratch[w];
+#pragma unroll
+  for (int width = NWARPS; width > 1; width >>= 1) {
+#pragma unroll
+    for (int i = 0; i < width / 2; ++i)
+      s[i] = make_float2(__fadd_rn(s[2 * i].x, s[2 * i + 1].x), __fadd_rn(s[2 * i].y, s[2 * i + 1].y));
+  }
+  __syncthreads();
+  return s[0];
+}
+
+template <int NWARPS>
+__device__ __forceinline__ float2 block_max2(float2 v, float2* scratch) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    v.x = fmaxf(v.x, __shfl_xor_sync(0xffffffffu, v.x, off));
+    v.y = fmaxf(v.y, __shfl_xor_sync(0xffffffffu, v.y, off));
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float2 m = scratch[0];
+#pragma unroll
+  for (int w = 1; w < NWARPS; ++w) m = make_float2(fmaxf(m.x, scratch[w].x), fmaxf(m.y, scratch[w].y));
+  __syncthreads();
+  return m;
+}
+
+template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
+__global__ void __launch_bounds__(kThreads) rms_mod2_kernel(const RmsArgs a) {
+  __shared__ float2 red[kWarps];
+  const int hidden = a.hidden;
+  const int64_t row0 = 2 * (int64_t)blockIdx.x;
+  const bool has1 = row0 + 1 < a.rows;
+  const int64_t rows2[2] = {row0, has1 ? row0 + 1 : row0};
+  uint4 v[2][C];
+  const bf16* trow[2];
+  bool have_table[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    bool bad;
+    trow[j] = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence, rows2[j], bad);
+    if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
+    have_table[j] = trow[j] != nullptr;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+      v[j][c] = load_chunk<VEC, true>(a.x + rows2[j] * (int64_t)hidden,
+                                      ((int64_t)c * kThreads + threadIdx.x) * 8, hidden);
+  }
+  if (RESID) {
+    // v = bf16(x + bf16(gate * update))   (model/kernels.py:101-105)
+    const uint4 gate_default = splat8(a.table == nullptr ? kBf2One : 0u);
+    uint4 d[2][C];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        d[j][c] = load_chunk<VEC, true>(a.update + rows2[j] * (int64_t)hidden,
+                                        ((int64_t)c * kThreads + threadIdx.x) * 8, hidden);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+        const uint4 gt = have_table[j]
+                             ? load_chunk<VEC, false>(trow[j] + (int64_t)a.gate_slot * hidden, col, hidden)
+                             : gate_default;
+        v[j][c] = badd8(v[j][c], bmul8(gt, d[j][c]));
+        if (j == 0 || has1) store_chunk<VEC>(a.residual_out + rows2[j] * (int64_t)hidden, col, hidden, v[j][c]);
+      }
+  }
+  // sum of squares per row: two running partials per thread (even / odd columns)
+  float part[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float2 p2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float f[8];
+      unpack8(v[j][c], f);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float2 x2 = make_float2(f[e], f[e + 1]);
+        p2 = __ffma2_rn(x2, x2, p2);
+      }
+    }
+    part[j] = __fadd_rn(p2.x, p2.y);
+  }
+  const float2 ss = block_sum2<kWarps>(make_float2(part[0], part[1]), red);
+  // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
+  const float rr[2] = {__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss.x, (float)hidden), a.eps))),
+                       __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss.y, (float)hidden), a.eps)))};
+  uint32_t amax2[2] = {0u, 0u};
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
+    float w[8];
+    unpack8(load_chunk<VEC, false>(a.weight, col, hidden), w);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float f[8];
+      unpack8(v[j][c], f);
+      const float2 r2 = make_float2(rr[j], rr[j]);
+      // n = bf16((x * r) * w)   (model/kernels.py:65-68,106-108)
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float2 n2 = __fmul2_rn(__fmul2_rn(make_float2(f[e], f[e + 1]), r2), make_float2(w[e], w[e + 1]));
+        f[e] = n2.x;
+        f[e + 1] = n2.y;
+      }
+      uint4 m = pack8(f);
+      if (MOD && have_table[j]) {
+        // m = bf16(bf16(n * bf16(1 + scale)) + shift)   (model/kernels.py:77-78,117-120)
+        const uint4 sc = load_chunk<VEC, false>(trow[j] + (int64_t)a.scale_slot * hidden, col, hidden);
+        const uint4 sh = load_chunk<VEC, false>(trow[j] + (int64_t)a.shift_slot * hidden, col, hidden);
+        m = badd8(bmul8(m, badd8(splat8(kBf2One), sc)), sh);
+      }
+      if (QUANT) amax2[j] = bamax8(amax2[j], m);
+      v[j][c] = m;
+    }
+  }
+  if (QUANT) {
+    const float2 amax = block_max2<kWarps>(make_float2(bamax_final(amax2[0]), bamax_final(amax2[1])), red);
+    const float am[2] = {amax.x, amax.y};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j == 1 && !has1) break;
+      const float s = row_scale_from_absmax(am[j]);
+      const float inv = __frcp_rn(s);
+      int8_t* dst = a.q + rows2[j] * (int64_t)hidden;
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        store_q8<VEC>(dst, ((int64_t)c * kThreads + threadIdx.x) * 8, hidden, quant8(v[j][c], s, inv));
+      if (threadIdx.x == 0) a.scales[rows2[j]] = s;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j == 1 && !has1) break;
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        store_chunk<VEC>(a.out + rows2[j] * (int64_t)hidden, ((int64_t)c * kThreads + threadIdx.x) * 8, hidden,
+                         v[j][c]);
+    }
   }
 }
 
@@ -567,10 +666,16 @@ static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, 
                       cudaStream_t s) {
   const int C = pick_chunks(a.hidden);
   if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln: hidden %d > 32768", a.hidden);
-#define LR_RMS(V, R, M, Q) \
-  lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(a)
+// The residual variant (K8) of rows of up to 4 chunks per thread runs two rows
+// per CTA (measured faster); every other case the persistent one-row kernel.
+// Both reduce each row in the same tree, so their results are identical.
+#define LR_RMS(V, R, M, Q)                                                                        \
+  if (R && kC <= 4)                                                                               \
+    lr::rms_mod2_kernel<(kC <= 4 ? kC : 4), V, R, M, Q><<<(unsigned)((rows + 1) / 2), lr::kThreads, 0, s>>>(a); \
+  else                                                                                            \
+    lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(a)
 #define LR_RMS_Q(V, R, M)  \
-  if (quant) LR_RMS(V, R, M, true); else LR_RMS(V, R, M, false)
+  if (quant) { LR_RMS(V, R, M, true); } else { LR_RMS(V, R, M, false); }
 #define LR_RMS_M(V, R)     \
   if (mod) { LR_RMS_Q(V, R, true); } else { LR_RMS_Q(V, R, false); }
 #define LR_RMS_R(V)        \
