@@ -115,6 +115,26 @@ int lr_swiglu(const void* projected, int64_t rows, int64_t inner, void* out, voi
 int lr_swiglu_quant_int8(const void* projected, int64_t rows, int64_t inner, int8_t* q,
                          float* scales, void* stream);
 
+/* K9 — per-head RMSNorm + rotary embedding of Q and K (the step after the QKV
+ * projection). Replaces the reference's `_qk_norm_full_rope_paired_kernel`
+ * (model/kernels.py:188-257) and `_qk_norm_rope_kernel` (:345-402) as launched
+ * by FusedAttention (model/fusion.py:29-54). For each (batch b, token t,
+ * head h) row of Q (and likewise K):
+ *   r = 1 / sqrt(sum_d x^2 / head_dim + eps);  n = bf16((x * r) * w)
+ *   d <  rotary_dim: out = bf16(bf16(n_d * c) + bf16(+-n_pair * s)),
+ *        c, s = bf16(cos[t, d]), bf16(sin[t, d]), pair = d -+ rotary_dim/2
+ *        (minus sign for the first half)
+ *   d >= rotary_dim: out = n_d
+ * query/key rows start at b*sequence*token_stride + t*token_stride +
+ * h*head_stride (bf16, unit element stride); cos/sin: fp32 [sequence,
+ * rotary_dim]; q_out/k_out: bf16 [batch, sequence, heads, head_dim] contiguous.
+ * head_dim <= 256, rotary_dim even and <= head_dim. */
+int lr_qk_norm_rope(const void* query, const void* key, int64_t q_token_stride,
+                    int64_t q_head_stride, int64_t k_token_stride, int64_t k_head_stride,
+                    const void* q_weight, const void* k_weight, const float* cos, const float* sin,
+                    int64_t batch, int64_t sequence, int64_t heads, int64_t head_dim,
+                    int64_t rotary_dim, float eps, void* q_out, void* k_out, void* stream);
+
 /* K10 (+K2 fused) — INT8 GEMM with int32 accumulation and a fused bf16 epilogue.
  * Replaces model/int8_gemm.py:200-267 `int8_matmul` (kernel `_gemm` :117-150),
  * model/int8_tma.py:299-308 `matmul`, and the GEMM inside

@@ -488,6 +488,73 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict
   }
 }
 
+// -------------------------------------------------------- Q/K RMSNorm + RoPE
+// One warp per (batch, token, head) row, first Q then K (model/kernels.py:
+// 188-257 full rotary, 345-402 general). Lane l holds elements l, l+32, ...;
+// the sum of squares is the lane's running sum over its elements followed by
+// the xor butterfly; the normalised row is staged in shared memory so each
+// lane can read its rotary partner (d +- rotary_dim/2) whatever the layout.
+template <int J>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, int64_t q_ts, int64_t q_hs, int64_t k_ts,
+    int64_t k_hs, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int64_t rows, int64_t sequence,
+    int heads, int head_dim, int rotary_dim, float eps, bf16* __restrict__ q_out,
+    bf16* __restrict__ k_out) {
+  __shared__ float buf[8][32 * J];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = rotary_dim / 2;
+  const uint16_t* wbits[2] = {reinterpret_cast<const uint16_t*>(wq), reinterpret_cast<const uint16_t*>(wk)};
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t token = (row / heads) % sequence;
+    const int64_t head = row % heads;
+    const int64_t batch = row / (sequence * heads);
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const int64_t ts = which ? k_ts : q_ts, hs = which ? k_hs : q_hs;
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(which ? k : q) + batch * sequence * ts +
+                            token * ts + head * hs;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(which ? k_out : q_out) + row * (int64_t)head_dim;
+      float x[J];
+      float part = 0.0f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int d = lane + 32 * j;
+        x[j] = d < head_dim ? bf_bits(src[d]) : 0.0f;
+        part = __fmaf_rn(x[j], x[j], part);  // exact square of a bf16 value
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
+      // r = 1 / sqrt(sum / head_dim + eps); n = bf16((x * r) * w)
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(part, (float)head_dim), eps)));
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int d = lane + 32 * j;
+        if (d < head_dim) {
+          x[j] = bf16r(__fmul_rn(__fmul_rn(x[j], r), bf_bits(wbits[which][d])));
+          buf[warp][d] = x[j];
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int d = lane + 32 * j;
+        if (d >= head_dim) continue;
+        float o = x[j];
+        if (d < rotary_dim) {
+          // bf16(bf16(n_d * cos_d) + bf16(+-n_pair * sin_d)), cos/sin rounded to bf16
+          const float c = bf16r(cos_t[token * rotary_dim + d]);
+          const float s = bf16r(sin_t[token * rotary_dim + d]);
+          const float p = d < half ? -buf[warp][d + half] : buf[warp][d - half];
+          o = bf16r(__fadd_rn(bf16r(__fmul_rn(x[j], c)), bf16r(__fmul_rn(p, s))));
+        }
+        dst[d] = f2bf_bits(o);
+      }
+      __syncwarp();
+    }
+  }
+}
+
 // --------------------------------------------------------------------- K2
 // One CTA per row; 4 int32 accumulators per thread step.
 template <bool VEC>
@@ -823,4 +890,41 @@ extern "C" int lr_swiglu_quant_int8(const void* projected, int64_t rows, int64_t
   if (rows > 0 && (q == nullptr || scales == nullptr))
     return lr::set_error(LR_ERR_INVALID_ARGUMENT, "swiglu_quant_int8: null output");
   return swiglu_common("swiglu_quant_int8", projected, rows, inner, nullptr, q, scales, stream);
+}
+
+extern "C" int lr_qk_norm_rope(const void* query, const void* key, int64_t q_token_stride,
+                               int64_t q_head_stride, int64_t k_token_stride, int64_t k_head_stride,
+                               const void* q_weight, const void* k_weight, const float* cos,
+                               const float* sin, int64_t batch, int64_t sequence, int64_t heads,
+                               int64_t head_dim, int64_t rotary_dim, float eps, void* q_out,
+                               void* k_out, void* stream) {
+  LR_REQUIRE(batch >= 0 && sequence >= 0 && heads > 0 && head_dim > 0, "qk_norm_rope: invalid shape");
+  LR_REQUIRE(head_dim <= 256, "qk_norm_rope: head_dim %lld > 256", (long long)head_dim);
+  LR_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0,
+             "rotary dimensions must be even and fit the attention head");
+  const int64_t rows = batch * sequence * heads;
+  if (rows == 0) return LR_OK;
+  LR_REQUIRE(query && key && q_weight && k_weight && q_out && k_out && (rotary_dim == 0 || (cos && sin)),
+             "qk_norm_rope: null pointer");
+  const int J = (int)((head_dim + 31) / 32);
+  const int64_t ctas = (rows + 7) / 8;
+  const unsigned grid = (unsigned)(ctas < 148 * 8 ? ctas : 148 * 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bf16 *qp = static_cast<const bf16*>(query), *kp = static_cast<const bf16*>(key);
+  const bf16 *wq = static_cast<const bf16*>(q_weight), *wk = static_cast<const bf16*>(k_weight);
+  bf16 *qo = static_cast<bf16*>(q_out), *ko = static_cast<bf16*>(k_out);
+#define LR_QK(JJ)                                                                                  \
+  lr::qk_norm_rope_kernel<JJ><<<grid, 256, 0, s>>>(qp, kp, q_token_stride, q_head_stride, k_token_stride, \
+                                                   k_head_stride, wq, wk, cos, sin, rows, sequence,      \
+                                                   (int)heads, (int)head_dim, (int)rotary_dim, eps, qo, ko)
+  switch (J) {
+    case 1: LR_QK(1); break;
+    case 2: LR_QK(2); break;
+    case 3: LR_QK(3); break;
+    case 4: LR_QK(4); break;
+    case 5: case 6: LR_QK(6); break;
+    default: LR_QK(8); break;
+  }
+#undef LR_QK
+  return lr::launch_status("qk_norm_rope");
 }

@@ -16,7 +16,7 @@ from ._lib import check, ptr, stream_of
 
 __all__ = [
     "quantize_rows", "int8_epilogue", "_rms_adaln", "_rms_adaln_quant_int8", "_gated_residual",
-    "_swiglu", "_swiglu_quant_int8", "residual_rms_quant",
+    "_swiglu", "_swiglu_quant_int8", "residual_rms_quant", "qk_norm_rope",
 ]
 
 
@@ -188,3 +188,37 @@ def _swiglu_quant_int8(projected):
     check(_lib.load().lr_swiglu_quant_int8(ptr(projected), rows, inner, ptr(output), ptr(scales),
                                            stream_of(projected)), "_swiglu_quant_int8")
     return output, scales
+
+
+def qk_norm_rope(query, key, norm_q, norm_k, rotary_emb):
+    """Per-head RMSNorm + rotary embedding of Q and K -> contiguous (q_out, k_out).
+
+    Replaces the launches of ``_qk_norm_full_rope_paired_kernel`` /
+    ``_qk_norm_rope_kernel`` in FusedAttention (model/fusion.py:29-54).
+    query, key: bf16 [B, S, H, D] (strided views of a fused QKV output are
+    fine); norm_q/norm_k: modules with .weight (bf16 [D]) and .eps;
+    rotary_emb: (cos, sin), each [S, rotary_dim].
+    """
+    cos, sin = rotary_emb
+    if cos is None or cos.ndim != 2:
+        raise ValueError("fused attention requires a padless rotary layout")
+    b, s, h, d = query.shape
+    rot = cos.shape[-1]
+    if rot > d or rot % 2:
+        raise ValueError("rotary dimensions must be even and fit the attention head")
+    _require_bf16("qk_norm_rope", query, key, norm_q.weight, norm_k.weight)
+
+    def layout(t):
+        if t.stride(-1) != 1 or (b > 1 and t.stride(0) != s * t.stride(1)):
+            t = t.contiguous()
+        return t
+    query, key = layout(query), layout(key)
+    cos = cos.to(torch.float32).contiguous()
+    sin = sin.to(torch.float32).contiguous()
+    q_out = torch.empty((b, s, h, d), device=query.device, dtype=torch.bfloat16)
+    k_out = torch.empty_like(q_out)
+    check(_lib.load().lr_qk_norm_rope(
+        ptr(query), ptr(key), query.stride(1), query.stride(2), key.stride(1), key.stride(2),
+        ptr(norm_q.weight.contiguous()), ptr(norm_k.weight.contiguous()), ptr(cos), ptr(sin), b, s, h, d, rot,
+        float(norm_q.eps), ptr(q_out), ptr(k_out), stream_of(query)), "qk_norm_rope")
+    return q_out, k_out

@@ -266,6 +266,80 @@ def swiglu_quant_int8(projected):
     return quantize_rows(swiglu(projected))
 
 
+# --------------------------------------------- Q/K RMSNorm + RoPE (next row)
+
+
+def sumsq_lane32(v: np.ndarray) -> np.ndarray:
+    """Row sum of squares in the order of the CUDA Q/K kernel (one warp per
+    head row): lane l adds the squares of elements l, l+32, l+64, ... in that
+    order, then the 32 lanes add by an xor butterfly (16, 8, 4, 2, 1)."""
+    v = np.asarray(v, F32)
+    rows, width = v.shape
+    chunks = max(1, -(-width // 32))
+    padded = np.zeros((rows, chunks * 32), F32)
+    padded[:, :width] = v
+    sq = (padded * padded).reshape(rows, chunks, 32)
+    lanes = np.zeros((rows, 32), F32)
+    for j in range(chunks):
+        lanes = lanes + sq[:, j, :]
+    idx = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        lanes = lanes + lanes[:, idx ^ off]
+    return lanes[:, 0]
+
+
+def sumsq_qk_reference(v: np.ndarray, rotary_dim: int, ordered: bool) -> np.ndarray:
+    """The reference Q/K kernels' sum order under the Triton interpreter:
+    full-rotary kernel sums (left^2 + right^2) over the half block
+    (model/kernels.py:217-222); the general kernel sums x^2 over the block
+    (:374-375), or, ordered, ((s0 + s2) + (s1 + s3)) over 32-wide quarters
+    (:332-343)."""
+    v = np.asarray(v, F32)
+    rows, width = v.shape
+    if rotary_dim == width:
+        half = width // 2
+        block = 1 << max(0, (half - 1).bit_length())
+        pair = np.zeros((rows, block), F32)
+        pair[:, :half] = v[:, :half] * v[:, :half] + v[:, half:] * v[:, half:]
+        return np.sum(pair, axis=-1, dtype=F32)
+    if ordered:
+        s = [np.sum(v[:, 32 * i:32 * (i + 1)] * v[:, 32 * i:32 * (i + 1)], axis=-1, dtype=F32) for i in range(4)]
+        return (s[0] + s[2]) + (s[1] + s[3])
+    block = 1 << max(0, (width - 1).bit_length())
+    padded = np.zeros((rows, block), F32)
+    padded[:, :width] = v
+    return np.sum(padded * padded, axis=-1, dtype=F32)
+
+
+def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=sumsq_lane32):
+    """Per-head RMSNorm + rotary embedding of one of Q or K
+    (model/kernels.py:188-257 full rotary, :345-402 general).
+
+    x: float32 [rows, head_dim] (bf16 values), one row per (batch, token, head);
+    tokens: int [rows], the token of each row (its cos/sin row);
+    cos, sin: float32 [sequence, rotary_dim]. Returns float32 [rows, head_dim]:
+      n = bf16((x * r) * w), r = 1 / sqrt(sum x^2 / head_dim + eps)
+      d < rotary_dim: bf16(bf16(n_d * c_d) + bf16(s_sign * n_pair * s_d)) with
+      c, s the bf16-rounded tables, pair = d +- rotary_dim/2, sign - then +;
+      d >= rotary_dim: n_d.
+    """
+    v = np.asarray(x, F32)
+    rows, width = v.shape
+    ss = reduce(v)
+    r = (F32(1) / np.sqrt(ss / F32(width) + F32(eps))).astype(F32)
+    n = bf16_round((v * r[:, None]) * np.asarray(weight, F32)[None, :])
+    out = n.copy()
+    half = rotary_dim // 2
+    c = bf16_round(np.asarray(cos, F32)[tokens])
+    s = bf16_round(np.asarray(sin, F32)[tokens])
+    d = np.arange(rotary_dim)
+    pair = np.where(d < half, d + half, d - half)
+    sign = np.where(d < half, F32(-1), F32(1))
+    rot = bf16_round(bf16_round(n[:, :rotary_dim] * c) + bf16_round((sign * n[:, pair]) * s))
+    out[:, :rotary_dim] = rot
+    return out
+
+
 # ---------------------------------------------------------- W8A8 linear
 
 

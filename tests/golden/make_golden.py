@@ -208,6 +208,36 @@ def main(reference_root: str) -> None:
     out["epi.y"] = bits(ref_k.int8_epilogue(acc, rs, cs, bias))
     out["epi.y_nobias"] = bits(ref_k.int8_epilogue(acc, rs, cs, None))
 
+    # ---- Q/K RMSNorm + RoPE (model/kernels.py:188-257, 331-402), called the way
+    # FusedAttention calls them (model/fusion.py:29-54): strided views into a
+    # fused QKV output, fp32 cos/sin tables [S, rotary_dim]
+    for name, (b, s, h, d, rot, ordered) in {"qk_full": (1, 5, 3, 128, 128, False),
+                                             "qk_part": (2, 4, 2, 128, 64, False),
+                                             "qk_ord": (1, 3, 2, 128, 32, True),
+                                             "qk_96": (1, 6, 2, 96, 48, False)}.items():
+        qkv = torch.randn(b, s, 3 * h * d, generator=g).to(torch.bfloat16)
+        q, kk, _ = [t.unflatten(-1, (h, -1)) for t in qkv.chunk(3, dim=-1)]
+        wq = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+        wk = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+        phase = torch.randn(s, rot, generator=g)
+        cos, sin = phase.cos(), phase.sin()
+        qo = torch.empty_like(q, memory_format=torch.contiguous_format)
+        ko = torch.empty_like(kk, memory_format=torch.contiguous_format)
+        common = (q, kk, wq, wk, cos, sin, qo, ko, s, h, q.stride(1), q.stride(2), kk.stride(1), kk.stride(2), d)
+        grid = (q.numel() // d,)
+        if rot == d:
+            ref_k._qk_norm_full_rope_paired_kernel[grid](*common, 1e-6, triton.next_power_of_2(d // 2),
+                                                         num_warps=4, enable_fp_fusion=False)
+        else:
+            ref_k._qk_norm_rope_kernel[grid](*common, rot, 1e-6, triton.next_power_of_2(d),
+                                             ordered_reduction=ordered, num_warps=1 if ordered else 4,
+                                             enable_fp_fusion=False)
+        out[f"{name}.qkv"] = bits(qkv)
+        out[f"{name}.wq"], out[f"{name}.wk"] = bits(wq), bits(wk)
+        out[f"{name}.cos"], out[f"{name}.sin"] = cos.numpy(), sin.numpy()
+        out[f"{name}.dims"] = np.array([b, s, h, d, rot, int(ordered)], np.int64)
+        out[f"{name}.qo"], out[f"{name}.ko"] = bits(qo), bits(ko)
+
     np.savez_compressed(HERE / "w8a8_small.npz", **out)
 
     # ---- full-size fingerprints (inputs regenerated from seeds) --------------

@@ -142,3 +142,19 @@ def test_quantize_transformer_report_shape():
     report = json.loads((GOLDEN / "quantize_transformer.json").read_text())
     assert report["quantized_blocks"] == [1, 2]
     assert report["quantized_linears"] == 8
+
+
+@pytest.mark.parametrize("name", ["qk_full", "qk_part", "qk_ord", "qk_96"])
+def test_qk_norm_rope_golden(g, name):
+    """The reference's Q/K RMSNorm+RoPE kernels (model/kernels.py:188-257,
+    331-402), run by the interpreter, equal the oracle in the interpreter's
+    sum order."""
+    b, s, h, d, rot, ordered = (int(v) for v in g[f"{name}.dims"])
+    qkv = f32(g[f"{name}.qkv"]).reshape(b, s, 3 * h * d)
+    q = qkv[..., :h * d].reshape(-1, d)
+    k = qkv[..., h * d:2 * h * d].reshape(-1, d)
+    tokens = (np.arange(b * s * h) // h) % s
+    for x, w, key in ((q, "wq", "qo"), (k, "wk", "ko")):
+        ref = O.qk_norm_rope(x, f32(g[f"{name}.{w}"]), 1e-6, g[f"{name}.cos"], g[f"{name}.sin"], rot, tokens,
+                             reduce=lambda v: O.sumsq_qk_reference(v, rot, bool(ordered)))
+        assert_bits(ref, g[f"{name}.{key}"].reshape(-1, d))
