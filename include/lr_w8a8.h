@@ -48,8 +48,9 @@ const char* lr_last_error(void);
 
 /* Read (and, if clear != 0, reset) the device status bits of the current device.
  * Bit 0: an adaLN index was outside [0, table_rows) (that row used a zero
- * modulation); bit 1: a bounded wait inside the GEMM gave up. Synchronises the
- * device. */
+ * modulation); bit 1: a bounded wait inside the GEMM gave up; bit 2: a row
+ * index of lr_gather_rows / lr_flash_restore was outside its source (that
+ * output row was written from zeros). Synchronises the device. */
 int lr_device_status(unsigned int* bits, int clear);
 
 /* K1 — per-row dynamic int8 quantisation.
@@ -134,6 +135,45 @@ int lr_qk_norm_rope(const void* query, const void* key, int64_t q_token_stride,
                     const void* q_weight, const void* k_weight, const float* cos, const float* sin,
                     int64_t batch, int64_t sequence, int64_t heads, int64_t head_dim,
                     int64_t rotary_dim, float eps, void* q_out, void* k_out, void* stream);
+
+/* F1 — row gather (the index_select calls of Flash token compression).
+ * Replaces the Tensor.index_select calls of model/flash.py:71-79 (hidden rows
+ * along the sequence, adaLN indices, rotary rows, attention-mask columns):
+ *   out[o, i, :] = src[o, index[i], :]   for o < outer, i < n_index,
+ * where a "row" is `row_bytes` contiguous bytes, src slice o starts at byte
+ * o * src_outer_stride and out slice o at byte o * out_outer_stride. Any
+ * element type: the copy is bytewise (16-byte vectors when sizes and pointers
+ * allow). An index outside [0, src_rows) sets status bit 2 and writes zeros. */
+int lr_gather_rows(const void* src, int64_t outer, int64_t src_outer_stride, int64_t src_rows,
+                   int64_t row_bytes, const int64_t* index, int64_t n_index, void* out,
+                   int64_t out_outer_stride, void* stream);
+
+/* F2 — Flash residual restore before the first full-resolution suffix block.
+ * Replaces the `restore` hook of model/flash.py:81-84 (a subtract, a scale,
+ * an index_select and an add over four tensors) with one pass:
+ *   k = inverse[t]
+ *   out[b,t,:] = bf16(full[b,t,:] + bf16(bf16(compressed[b,k,:] - input[b,k,:]) * gain))
+ * full, out: bf16 [batch, sequence, hidden]; compressed (the last compressed
+ * block's output) and input (the compressed sequence that entered the first
+ * compressed block): bf16 [batch, kept, hidden]; inverse: int64 [sequence].
+ * out may alias full. */
+int lr_flash_restore(const void* full, const void* compressed, const void* input,
+                     const int64_t* inverse, int64_t batch, int64_t sequence, int64_t kept,
+                     int64_t hidden, float gain, void* out, void* stream);
+
+/* F3 — nearest same-time anchor of every dropped video row (the cdist/argmin
+ * loop of spatial_layout, model/flash.py:27-32):
+ *   for r < n_dropped: src = dropped[r];
+ *     best = argmin over j with positions[anchors[j],0] == positions[src,0] of
+ *            |positions[src,1:3] - positions[anchors[j],1:3]|  (first j on ties;
+ *            0 if no anchor shares the time);
+ *     inverse[src] = inverse[anchors[best]]
+ * positions: fp32 [sequence, 3] (time, row, column); the distance is the fp32
+ * square root of the squared distance, which equals the reference's fp32
+ * cdist wherever that is exact (integer coordinates below 2^11). */
+int lr_flash_nearest_anchor(const float* positions, int64_t sequence, const int64_t* dropped,
+                            int64_t n_dropped, const int64_t* anchors, int64_t n_anchors,
+                            int64_t* inverse, void* stream);
 
 /* K10 (+K2 fused) — INT8 GEMM with int32 accumulation and a fused bf16 epilogue.
  * Replaces model/int8_gemm.py:200-267 `int8_matmul` (kernel `_gemm` :117-150),

@@ -44,6 +44,9 @@ SIGNATURES = {
     "lr_swiglu_quant_int8": ([_p, _i64, _i64, _p, _p, _p], _i32),
     "lr_qk_norm_rope": ([_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f32,
                          _p, _p, _p], _i32),
+    "lr_gather_rows": ([_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p], _i32),
+    "lr_flash_restore": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p, _p], _i32),
+    "lr_flash_nearest_anchor": ([_p, _i64, _p, _i64, _p, _i64, _p, _p], _i32),
     "lr_int8_gemm": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
                       _i64, _i64, _p, _i64, _i32, _p, _i64, _p], _i32),
     "lr_int8_gemm_workspace_bytes": ([_i64, _i64, _i64], _i64),

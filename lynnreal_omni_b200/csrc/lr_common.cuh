@@ -34,6 +34,7 @@ namespace lr {
 enum : unsigned int {
   kDevErrTableIndex = 1u << 0,  // an adaLN index pointed outside the table
   kDevErrWaitTimeout = 1u << 1, // a bounded mbarrier wait gave up
+  kDevErrRowIndex = 1u << 2,    // a gather/restore row index pointed outside its source
 };
 
 // ------------------------------------------------------- scalar bf16 helpers

@@ -489,19 +489,108 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict
 }
 
 // -------------------------------------------------------- Q/K RMSNorm + RoPE
-// One warp per (batch, token, head) row, first Q then K (model/kernels.py:
-// 188-257 full rotary, 345-402 general). Lane l holds elements l, l+32, ...;
-// the sum of squares is the lane's running sum over its elements followed by
-// the xor butterfly; the normalised row is staged in shared memory so each
-// lane can read its rotary partner (d +- rotary_dim/2) whatever the layout.
-template <int J>
-__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+// model/kernels.py:188-257 (full rotary) and :345-402 (general), per head row:
+//   r = 1 / sqrt(sum(x^2) / head_dim + eps);  n = bf16((x * r) * w)
+//   d < rotary_dim: bf16(bf16(n_d * c_d) + bf16(-+n_pair * s_d)), c/s the
+//   bf16-rounded cos/sin of the row's token, pair = d +- rotary_dim / 2.
+// One sum order for both kernels below: with L = next power of two >=
+// ceil(head_dim / 8) lanes per row, lane l holds elements [8l, 8l + 8), sums
+// the squares of its even and of its odd elements (left to right), adds the
+// two, and the L lanes add by an xor butterfly (L/2, ..., 1).
+
+// Fast form: one CTA per token, heads contiguous (head stride = head_dim),
+// 16-byte aligned rows, head_dim = 8L with L a power of two <= 32, rotary_dim
+// 0 or 16 * 2^k. Thread t owns chunk position p = t % L of every head it
+// touches (256 is a multiple of L), so its weights and cos/sin are loaded once
+// per token; the rotary partner chunk is lane p ^ (rotary_dim / 16) of the
+// same head. All NI chunk loads of a thread are issued before any compute.
+template <int NI>
+__global__ void __launch_bounds__(256) qk_norm_rope_tok_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, int64_t q_ts, int64_t k_ts,
+    const bf16* __restrict__ wq, const bf16* __restrict__ wk, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int64_t sequence, int qc, int lanes, int head_dim, int rotary_dim,
+    float eps, bf16* __restrict__ q_out, bf16* __restrict__ k_out) {
+  const int64_t tok = blockIdx.x;
+  const int64_t b = tok / sequence, s = tok - b * sequence;
+  const int t = threadIdx.x;
+  const int p = t & (lanes - 1);
+  uint4 x[NI];
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    const int c = t + 256 * i;
+    if (c < 2 * qc) {
+      const bool is_k = c >= qc;
+      const int cc = is_k ? c - qc : c;
+      const bf16* src = is_k ? k + (b * sequence + s) * k_ts : q + (b * sequence + s) * q_ts;
+      x[i] = ld_stream(src + (int64_t)cc * 8);
+    } else {
+      x[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  float wqf[8], wkf[8];
+  unpack8(ld_keep(wq + p * 8), wqf);
+  unpack8(ld_keep(wk + p * 8), wkf);
+  const bool rotates = p * 8 < rotary_dim;
+  const bool lower = p * 8 < rotary_dim / 2;
+  const int pair = rotary_dim / 16;
+  uint4 c2 = make_uint4(0u, 0u, 0u, 0u), s2 = c2;
+  if (rotates) {
+    const float4* cp = reinterpret_cast<const float4*>(cos_t + s * rotary_dim + p * 8);
+    const float4* sp = reinterpret_cast<const float4*>(sin_t + s * rotary_dim + p * 8);
+    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    c2 = make_uint4(cvt2(c0.x, c0.y), cvt2(c0.z, c0.w), cvt2(c1.x, c1.y), cvt2(c1.z, c1.w));
+    s2 = make_uint4(cvt2(s0.x, s0.y), cvt2(s0.z, s0.w), cvt2(s1.x, s1.y), cvt2(s1.z, s1.w));
+  }
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    const int c = t + 256 * i;
+    const bool is_k = c >= qc;
+    float f[8];
+    unpack8(x[i], f);
+    float2 part = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 v2 = make_float2(f[e], f[e + 1]);
+      part = __ffma2_rn(v2, v2, part);  // squares of bf16 values are exact
+    }
+    float ss = __fadd_rn(part.x, part.y);
+    for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)head_dim), eps)));
+    const float2 r2 = make_float2(r, r);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 n2 = __fmul2_rn(__fmul2_rn(make_float2(f[e], f[e + 1]), r2),
+                                   is_k ? make_float2(wkf[e], wkf[e + 1]) : make_float2(wqf[e], wqf[e + 1]));
+      f[e] = n2.x;
+      f[e + 1] = n2.y;
+    }
+    uint4 n = pack8(f);
+    if (rotary_dim > 0) {
+      uint4 m = make_uint4(__shfl_xor_sync(0xffffffffu, n.x, pair), __shfl_xor_sync(0xffffffffu, n.y, pair),
+                           __shfl_xor_sync(0xffffffffu, n.z, pair), __shfl_xor_sync(0xffffffffu, n.w, pair));
+      if (rotates) {
+        if (lower) m = make_uint4(m.x ^ 0x80008000u, m.y ^ 0x80008000u, m.z ^ 0x80008000u, m.w ^ 0x80008000u);
+        n = badd8(bmul8(n, c2), bmul8(m, s2));
+      }
+    }
+    if (c < 2 * qc) {
+      const int cc = is_k ? c - qc : c;
+      *reinterpret_cast<uint4*>((is_k ? k_out : q_out) + tok * (int64_t)qc * 8 + (int64_t)cc * 8) = n;
+    }
+  }
+}
+
+// General form (any head/token strides and alignment, head_dim <= 256, any
+// even rotary_dim): one warp per (batch, token, head) row, Q then K, element
+// loads; the normalised row is staged in shared memory so each lane can read
+// its rotary partner wherever it lies.
+__global__ void __launch_bounds__(256) qk_norm_rope_row_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, int64_t q_ts, int64_t q_hs, int64_t k_ts,
     int64_t k_hs, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int64_t rows, int64_t sequence,
-    int heads, int head_dim, int rotary_dim, float eps, bf16* __restrict__ q_out,
+    int heads, int head_dim, int lanes, int rotary_dim, float eps, bf16* __restrict__ q_out,
     bf16* __restrict__ k_out) {
-  __shared__ float buf[8][32 * J];
+  __shared__ float buf[8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = rotary_dim / 2;
   const uint16_t* wbits[2] = {reinterpret_cast<const uint16_t*>(wq), reinterpret_cast<const uint16_t*>(wk)};
@@ -515,38 +604,37 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       const uint16_t* src = reinterpret_cast<const uint16_t*>(which ? k : q) + batch * sequence * ts +
                             token * ts + head * hs;
       uint16_t* dst = reinterpret_cast<uint16_t*>(which ? k_out : q_out) + row * (int64_t)head_dim;
-      float x[J];
-      float part = 0.0f;
+      float x[8];
+      float ev = 0.0f, od = 0.0f;
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int d = lane + 32 * j;
-        x[j] = d < head_dim ? bf_bits(src[d]) : 0.0f;
-        part = __fmaf_rn(x[j], x[j], part);  // exact square of a bf16 value
+      for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
+        x[e] = d < head_dim ? bf_bits(src[d]) : 0.0f;
+        if (e & 1) od = __fmaf_rn(x[e], x[e], od);  // exact square of a bf16 value
+        else ev = __fmaf_rn(x[e], x[e], ev);
       }
+      float ss = __fadd_rn(ev, od);
+      for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)head_dim), eps)));
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
-      // r = 1 / sqrt(sum / head_dim + eps); n = bf16((x * r) * w)
-      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(part, (float)head_dim), eps)));
-#pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int d = lane + 32 * j;
+      for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
         if (d < head_dim) {
-          x[j] = bf16r(__fmul_rn(__fmul_rn(x[j], r), bf_bits(wbits[which][d])));
-          buf[warp][d] = x[j];
+          x[e] = bf16r(__fmul_rn(__fmul_rn(x[e], r), bf_bits(wbits[which][d])));
+          buf[warp][d] = x[e];
         }
       }
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int d = lane + 32 * j;
+      for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
         if (d >= head_dim) continue;
-        float o = x[j];
+        float o = x[e];
         if (d < rotary_dim) {
-          // bf16(bf16(n_d * cos_d) + bf16(+-n_pair * sin_d)), cos/sin rounded to bf16
           const float c = bf16r(cos_t[token * rotary_dim + d]);
-          const float s = bf16r(sin_t[token * rotary_dim + d]);
-          const float p = d < half ? -buf[warp][d + half] : buf[warp][d - half];
-          o = bf16r(__fadd_rn(bf16r(__fmul_rn(x[j], c)), bf16r(__fmul_rn(p, s))));
+          const float sn = bf16r(sin_t[token * rotary_dim + d]);
+          const float pv = d < half ? -buf[warp][d + half] : buf[warp][d - half];
+          o = bf16r(__fadd_rn(bf16r(__fmul_rn(x[e], c)), bf16r(__fmul_rn(pv, sn))));
         }
         dst[d] = f2bf_bits(o);
       }
@@ -906,25 +994,41 @@ extern "C" int lr_qk_norm_rope(const void* query, const void* key, int64_t q_tok
   if (rows == 0) return LR_OK;
   LR_REQUIRE(query && key && q_weight && k_weight && q_out && k_out && (rotary_dim == 0 || (cos && sin)),
              "qk_norm_rope: null pointer");
-  const int J = (int)((head_dim + 31) / 32);
-  const int64_t ctas = (rows + 7) / 8;
-  const unsigned grid = (unsigned)(ctas < 148 * 8 ? ctas : 148 * 8);
+  int lanes = 1;
+  while (lanes * 8 < head_dim) lanes *= 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bf16 *qp = static_cast<const bf16*>(query), *kp = static_cast<const bf16*>(key);
   const bf16 *wq = static_cast<const bf16*>(q_weight), *wk = static_cast<const bf16*>(k_weight);
   bf16 *qo = static_cast<bf16*>(q_out), *ko = static_cast<bf16*>(k_out);
-#define LR_QK(JJ)                                                                                  \
-  lr::qk_norm_rope_kernel<JJ><<<grid, 256, 0, s>>>(qp, kp, q_token_stride, q_head_stride, k_token_stride, \
-                                                   k_head_stride, wq, wk, cos, sin, rows, sequence,      \
-                                                   (int)heads, (int)head_dim, (int)rotary_dim, eps, qo, ko)
-  switch (J) {
-    case 1: LR_QK(1); break;
-    case 2: LR_QK(2); break;
-    case 3: LR_QK(3); break;
-    case 4: LR_QK(4); break;
-    case 5: case 6: LR_QK(6); break;
-    default: LR_QK(8); break;
-  }
+  const int64_t qc = heads * head_dim / 8;  // 16-byte chunks of one token's Q heads
+  const int64_t ni = (2 * qc + 255) / 256;
+  const bool rot_ok = rotary_dim == 0 || (rotary_dim % 16 == 0 && ((rotary_dim / 16) & (rotary_dim / 16 - 1)) == 0);
+  const bool fast = lanes * 8 == head_dim && q_head_stride == head_dim && k_head_stride == head_dim && rot_ok &&
+                    ni <= 16 && (q_token_stride * 2) % 16 == 0 && (k_token_stride * 2) % 16 == 0 &&
+                    lr::aligned(query, 16) && lr::aligned(key, 16) && lr::aligned(q_weight, 16) &&
+                    lr::aligned(k_weight, 16) && lr::aligned(q_out, 16) && lr::aligned(k_out, 16) &&
+                    (rotary_dim == 0 || (lr::aligned(cos, 16) && lr::aligned(sin, 16)));
+  if (fast) {
+    const unsigned grid = (unsigned)(batch * sequence);
+#define LR_QK(NN)                                                                                      \
+  lr::qk_norm_rope_tok_kernel<NN><<<grid, 256, 0, s>>>(qp, kp, q_token_stride, k_token_stride, wq, wk, cos, \
+                                                       sin, sequence, (int)qc, lanes, (int)head_dim,        \
+                                                       (int)rotary_dim, eps, qo, ko)
+    if (ni <= 1) LR_QK(1);
+    else if (ni <= 2) LR_QK(2);
+    else if (ni <= 3) LR_QK(3);
+    else if (ni <= 4) LR_QK(4);
+    else if (ni <= 6) LR_QK(6);
+    else if (ni <= 8) LR_QK(8);
+    else if (ni <= 12) LR_QK(12);
+    else LR_QK(16);
 #undef LR_QK
+  } else {
+    const int64_t ctas = (rows + 7) / 8;
+    const int64_t cap = 8ll * lr::sm_count();
+    lr::qk_norm_rope_row_kernel<<<(unsigned)(ctas < cap ? ctas : cap), 256, 0, s>>>(
+        qp, kp, q_token_stride, q_head_stride, k_token_stride, k_head_stride, wq, wk, cos, sin, rows, sequence,
+        (int)heads, (int)head_dim, lanes, (int)rotary_dim, eps, qo, ko);
+  }
   return lr::launch_status("qk_norm_rope");
 }

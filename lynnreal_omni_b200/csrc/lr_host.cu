@@ -40,6 +40,7 @@ int sm_count() {
 
 int read_status_elementwise(unsigned int* bits, int clear);
 int read_status_gemm(unsigned int* bits, int clear);
+int read_status_flash(unsigned int* bits, int clear);
 
 }  // namespace lr
 
@@ -53,5 +54,7 @@ extern "C" int lr_device_status(unsigned int* bits, int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return lr::launch_status("device_status: synchronize");
   int st = lr::read_status_elementwise(bits, clear);
   if (st) return st;
-  return lr::read_status_gemm(bits, clear);
+  st = lr::read_status_gemm(bits, clear);
+  if (st) return st;
+  return lr::read_status_flash(bits, clear);
 }

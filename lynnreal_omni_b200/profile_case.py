@@ -4,6 +4,11 @@
     python -m lynnreal_omni_b200.profile_case rms --m 12240 --d 6144
     python -m lynnreal_omni_b200.profile_case quant --m 12240 --d 24576
     python -m lynnreal_omni_b200.profile_case gated --m 12240 --d 6144
+    python -m lynnreal_omni_b200.profile_case qk --m 12240 --d 6144
+    python -m lynnreal_omni_b200.profile_case compress --d 6144   (21 x 48 x 64 video grid)
+    python -m lynnreal_omni_b200.profile_case restore --d 6144
+    python -m lynnreal_omni_b200.profile_case restore_torch --d 6144   (the reference's tensor ops)
+    python -m lynnreal_omni_b200.profile_case layout
 
 Each case launches its kernel ``--iters`` times on cuda:0 and prints the mean
 CUDA-event time per launch and the algorithmic rate (TOP/s or GB/s).
@@ -46,7 +51,8 @@ def _time(fn, iters: int, warmup: int, graph: bool = False):
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("case", choices=["gemm", "rms", "quant", "gated", "residual_rms"])
+    p.add_argument("case", choices=["gemm", "rms", "quant", "gated", "residual_rms", "qk", "compress", "restore",
+                                    "restore_torch", "layout"])
     p.add_argument("--m", type=int, default=12240)
     p.add_argument("--k", type=int, default=6144)
     p.add_argument("--n", type=int, default=24576)
@@ -80,6 +86,41 @@ def main(argv=None):
         ms = _time(fn, a.iters, a.warmup, a.graph)
         out.update(m=a.m, k=a.k, n=a.n, epi=a.epi, ms=ms, tops=2.0 * a.m * a.n * a.k / (ms / 1e3) / 1e12,
                    algorithmic_bytes=a.m * a.k + a.n * a.k + 2 * a.m * a.n + 4 * a.m + 6 * a.n)
+    elif a.case == "qk":
+        heads, hd = a.d // 128, 128
+        qkv = torch.randn(1, a.m, 3 * a.d, device=dev, generator=g).to(torch.bfloat16)
+        q, k, _ = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+        nq = SimpleNamespace(weight=torch.ones(hd, device=dev, dtype=torch.bfloat16), eps=1e-6)
+        phase = torch.randn(a.m, hd, device=dev, generator=g)
+        rot = (phase.cos(), phase.sin())
+        ms = _time(lambda: K.qk_norm_rope(q, k, nq, nq, rot), a.iters, a.warmup, a.graph)
+        nbytes = 8 * a.m * a.d + 8 * a.m * hd + 4 * hd
+        out.update(m=a.m, d=a.d, heads=heads, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    elif a.case in ("compress", "restore", "restore_torch", "layout"):
+        from . import flash
+        t, h, w = torch.meshgrid(torch.arange(21), torch.arange(48), torch.arange(64), indexing="ij")
+        pos = torch.stack([t, h, w], -1).reshape(-1, 3).to(dev)
+        tags = torch.zeros(pos.shape[0], dtype=torch.int64, device=dev)
+        keep, inverse = flash.spatial_layout(pos, tags)
+        s, kept = pos.shape[0], keep.numel()
+        if a.case == "layout":
+            ms = _time(lambda: flash.spatial_layout(pos, tags), a.iters, a.warmup, False)
+            out.update(rows=s, kept=kept, ms=ms)
+        else:
+            full = torch.randn(1, s, a.d, device=dev, generator=g).to(torch.bfloat16)
+            if a.case == "compress":
+                fn = lambda: flash.index_select(full, 1, keep)  # noqa: E731
+                nbytes = 4 * kept * a.d + 8 * kept
+            else:
+                comp = torch.randn(1, kept, a.d, device=dev, generator=g).to(torch.bfloat16)
+                inp = torch.randn(1, kept, a.d, device=dev, generator=g).to(torch.bfloat16)
+                if a.case == "restore":
+                    fn = lambda: flash.restore(full, comp, inp, inverse, 1.0)  # noqa: E731
+                else:
+                    fn = lambda: full + ((comp - inp) * 1.0).index_select(1, inverse)  # noqa: E731
+                nbytes = 4 * s * a.d + 4 * kept * a.d + 8 * s
+            ms = _time(fn, a.iters, a.warmup, a.graph)
+            out.update(rows=s, kept=kept, d=a.d, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
     else:
         x = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)
         y = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)

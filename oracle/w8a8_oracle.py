@@ -269,23 +269,27 @@ def swiglu_quant_int8(projected):
 # --------------------------------------------- Q/K RMSNorm + RoPE (next row)
 
 
-def sumsq_lane32(v: np.ndarray) -> np.ndarray:
-    """Row sum of squares in the order of the CUDA Q/K kernel (one warp per
-    head row): lane l adds the squares of elements l, l+32, l+64, ... in that
-    order, then the 32 lanes add by an xor butterfly (16, 8, 4, 2, 1)."""
+def sumsq_chunk8(v: np.ndarray) -> np.ndarray:
+    """Row sum of squares in the order of the CUDA Q/K kernels: with
+    L = next power of two >= ceil(width / 8) lanes per head row, lane l holds
+    elements [8l, 8l + 8) and sums the squares of its even and of its odd
+    elements separately, left to right, then adds the two; the L lanes then add
+    by an xor butterfly (L/2, ..., 2, 1). Missing elements count as zero."""
     v = np.asarray(v, F32)
     rows, width = v.shape
-    chunks = max(1, -(-width // 32))
-    padded = np.zeros((rows, chunks * 32), F32)
+    lanes = 1 << max(0, (-(-width // 8) - 1).bit_length())
+    padded = np.zeros((rows, lanes * 8), F32)
     padded[:, :width] = v
-    sq = (padded * padded).reshape(rows, chunks, 32)
-    lanes = np.zeros((rows, 32), F32)
-    for j in range(chunks):
-        lanes = lanes + sq[:, j, :]
-    idx = np.arange(32)
-    for off in (16, 8, 4, 2, 1):
-        lanes = lanes + lanes[:, idx ^ off]
-    return lanes[:, 0]
+    sq = (padded * padded).reshape(rows, lanes, 8)
+    even = ((sq[:, :, 0] + sq[:, :, 2]) + sq[:, :, 4]) + sq[:, :, 6]
+    odd = ((sq[:, :, 1] + sq[:, :, 3]) + sq[:, :, 5]) + sq[:, :, 7]
+    acc = even + odd
+    idx = np.arange(lanes)
+    off = lanes // 2
+    while off:
+        acc = acc + acc[:, idx ^ off]
+        off //= 2
+    return acc[:, 0]
 
 
 def sumsq_qk_reference(v: np.ndarray, rotary_dim: int, ordered: bool) -> np.ndarray:
@@ -311,7 +315,7 @@ def sumsq_qk_reference(v: np.ndarray, rotary_dim: int, ordered: bool) -> np.ndar
     return np.sum(padded * padded, axis=-1, dtype=F32)
 
 
-def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=sumsq_lane32):
+def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=sumsq_chunk8):
     """Per-head RMSNorm + rotary embedding of one of Q or K
     (model/kernels.py:188-257 full rotary, :345-402 general).
 

@@ -1,7 +1,7 @@
 """GPU tests of the Q/K RMSNorm+RoPE kernel and of the fused-block caller.
 
-Q/K bar: bit-exact against the oracle evaluated in the kernel's documented
-sum order (lane-strided sums + warp butterfly); against the reference's own
+Q/K bar: bit-exact against the oracle evaluated in the kernels' documented
+sum order (8-element chunks per lane + xor butterfly); against the reference's own
 kernels (golden vectors; their sums run in another order) at most 1 bf16 ulp
 on at most 0.5 % of the elements.
 
@@ -90,6 +90,25 @@ def test_qk_norm_rope_shapes(b, s, h, d, rot):
         rows = x[..., part * h * d:(part + 1) * h * d].reshape(-1, d)
         ref = O.qk_norm_rope(rows, O.to_numpy_f32(w), 1e-6, phase.cos().numpy(), phase.sin().numpy(), rot, tokens)
         np.testing.assert_array_equal(bits(out).reshape(-1, d), O.bf16_bits(ref))
+
+
+@pytest.mark.parametrize("d,rot", [(128, 128), (64, 32), (256, 0)])
+def test_qk_general_layout_equals_fast_layout(d, rot):
+    """Head rows with padding between heads take the general kernel; its sum
+    order is the fast kernel's, so the bits agree."""
+    b, s, h = 2, 7, 5
+    gen = torch.Generator().manual_seed(d + rot)
+    qkv = torch.randn(b, s, 3 * h * d, generator=gen).to(torch.bfloat16).to(DEV)
+    q, k, _ = [t.unflatten(-1, (h, -1)) for t in qkv.chunk(3, dim=-1)]
+    padded = torch.zeros(2, b, s, h, d + 8, dtype=torch.bfloat16, device=DEV)
+    padded[0, ..., :d], padded[1, ..., :d] = q, k
+    norm = SimpleNamespace(weight=(1 + 0.1 * torch.randn(d, generator=gen)).to(torch.bfloat16).to(DEV), eps=1e-6)
+    phase = torch.randn(s, rot, generator=gen).to(DEV)
+    rope = (phase.cos(), phase.sin())
+    fast = K.qk_norm_rope(q, k, norm, norm, rope)
+    general = K.qk_norm_rope(padded[0, ..., :d], padded[1, ..., :d], norm, norm, rope)
+    for a, c in zip(fast, general):
+        assert torch.equal(a, c)
 
 
 def test_qk_norm_rope_rejects_odd_rotary():

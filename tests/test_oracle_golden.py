@@ -118,6 +118,14 @@ def test_tree_sum_is_a_sum():
         np.testing.assert_allclose(O.sumsq_tree(v), exact, rtol=2e-6)
 
 
+def test_chunk8_sum_is_a_sum():
+    rng = np.random.default_rng(3)
+    for width in (8, 64, 96, 128, 256):
+        v = O.bf16_round(rng.standard_normal((5, width)).astype(np.float32))
+        exact = np.sum(v.astype(np.float64) ** 2, axis=1)
+        np.testing.assert_allclose(O.sumsq_chunk8(v), exact, rtol=2e-6)
+
+
 def test_bf16_rounding_matches_torch():
     rng = np.random.default_rng(2)
     v = (rng.standard_normal(100000) * np.exp(rng.uniform(-20, 20, 100000))).astype(np.float32)
