@@ -50,7 +50,8 @@ const char* lr_last_error(void);
  * Bit 0: an adaLN index was outside [0, table_rows) (that row used a zero
  * modulation); bit 1: a bounded wait inside the GEMM gave up; bit 2: a row
  * index of lr_gather_rows / lr_flash_restore was outside its source (that
- * output row was written from zeros). Synchronises the device. */
+ * output row was written from zeros). Bit 1 also covers the attention
+ * kernel's bounded waits. Synchronises the device. */
 int lr_device_status(unsigned int* bits, int clear);
 
 /* K1 — per-row dynamic int8 quantisation.
@@ -174,6 +175,22 @@ int lr_flash_restore(const void* full, const void* compressed, const void* input
 int lr_flash_nearest_anchor(const float* positions, int64_t sequence, const int64_t* dropped,
                             int64_t n_dropped, const int64_t* anchors, int64_t n_anchors,
                             int64_t* inverse, void* stream);
+
+/* A1 — attention core (bf16): for every batch b, query i, head h
+ *   out[b,i,h,:] = sum_j softmax_j(scale * q[b,i,h,:] . k[b,j,h,:]) * v[b,j,h,:]
+ * with fp32 scores and an fp32 online softmax (exp2), probabilities rounded to
+ * bf16 for the second product, bf16 output. Stands in for the attention
+ * backend FusedAttention calls between the Q/K RMSNorm+RoPE and the output
+ * projection (model/fusion.py:55-57; the reference calls diffusers'
+ * dispatch_attention_fn, i.e. a library SDPA kernel). No mask, not causal.
+ * q, k, v, out: bf16 [batch, seq, heads, head_dim] with heads contiguous inside
+ * a token and token strides in elements (a fused QKV output's views work
+ * as they are); head_dim must be 128; pointers and token strides 16-byte
+ * aligned (LR_ERR_UNSUPPORTED otherwise). */
+int lr_attention_bf16(const void* q, int64_t q_token_stride, const void* k, int64_t k_token_stride,
+                      const void* v, int64_t v_token_stride, int64_t batch, int64_t seq_q, int64_t seq_kv,
+                      int64_t heads, int64_t head_dim, float scale, void* out, int64_t out_token_stride,
+                      void* stream);
 
 /* K10 (+K2 fused) — INT8 GEMM with int32 accumulation and a fused bf16 epilogue.
  * Replaces model/int8_gemm.py:200-267 `int8_matmul` (kernel `_gemm` :117-150),

@@ -47,6 +47,7 @@ SIGNATURES = {
     "lr_gather_rows": ([_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p], _i32),
     "lr_flash_restore": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _p, _p], _i32),
     "lr_flash_nearest_anchor": ([_p, _i64, _p, _i64, _p, _i64, _p, _p], _i32),
+    "lr_attention_bf16": ([_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _p], _i32),
     "lr_int8_gemm": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
                       _i64, _i64, _p, _i64, _i32, _p, _i64, _p], _i32),
     "lr_int8_gemm_workspace_bytes": ([_i64, _i64, _i64], _i64),

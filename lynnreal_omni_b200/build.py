@@ -15,7 +15,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 LIBRARY = PACKAGE / "liblr_w8a8.so"
-SOURCES = ["lr_host.cu", "lr_elementwise.cu", "lr_gemm_sm100.cu", "lr_flash.cu"]
+SOURCES = ["lr_host.cu", "lr_elementwise.cu", "lr_gemm_sm100.cu", "lr_flash.cu", "lr_attention.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
          "-Xptxas", "-O3"]

@@ -41,6 +41,7 @@ int sm_count() {
 int read_status_elementwise(unsigned int* bits, int clear);
 int read_status_gemm(unsigned int* bits, int clear);
 int read_status_flash(unsigned int* bits, int clear);
+int read_status_attention(unsigned int* bits, int clear);
 
 }  // namespace lr
 
@@ -56,5 +57,7 @@ extern "C" int lr_device_status(unsigned int* bits, int clear) {
   if (st) return st;
   st = lr::read_status_gemm(bits, clear);
   if (st) return st;
-  return lr::read_status_flash(bits, clear);
+  st = lr::read_status_flash(bits, clear);
+  if (st) return st;
+  return lr::read_status_attention(bits, clear);
 }

@@ -9,6 +9,8 @@
     python -m lynnreal_omni_b200.profile_case restore --d 6144
     python -m lynnreal_omni_b200.profile_case restore_torch --d 6144   (the reference's tensor ops)
     python -m lynnreal_omni_b200.profile_case layout
+    python -m lynnreal_omni_b200.profile_case attn --m 12240 --d 6144   (48 heads x 128)
+    python -m lynnreal_omni_b200.profile_case attn_sdpa --m 12240 --d 6144   (torch SDPA, same inputs)
 
 Each case launches its kernel ``--iters`` times on cuda:0 and prints the mean
 CUDA-event time per launch and the algorithmic rate (TOP/s or GB/s).
@@ -52,7 +54,7 @@ def _time(fn, iters: int, warmup: int, graph: bool = False):
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("case", choices=["gemm", "rms", "quant", "gated", "residual_rms", "qk", "compress", "restore",
-                                    "restore_torch", "layout"])
+                                    "restore_torch", "layout", "attn", "attn_sdpa"])
     p.add_argument("--m", type=int, default=12240)
     p.add_argument("--k", type=int, default=6144)
     p.add_argument("--n", type=int, default=24576)
@@ -96,6 +98,19 @@ def main(argv=None):
         ms = _time(lambda: K.qk_norm_rope(q, k, nq, nq, rot), a.iters, a.warmup, a.graph)
         nbytes = 8 * a.m * a.d + 8 * a.m * hd + 4 * hd
         out.update(m=a.m, d=a.d, heads=heads, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    elif a.case in ("attn", "attn_sdpa"):
+        from .attention import attention_bshd
+        heads = a.d // 128
+        qkv = torch.randn(1, a.m, 3 * a.d, device=dev, generator=g).to(torch.bfloat16)
+        q, k, v = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+        if a.case == "attn":
+            fn = lambda: attention_bshd(q, k, v)  # noqa: E731
+        else:
+            qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+            fn = lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)  # noqa: E731
+        ms = _time(fn, a.iters, a.warmup, a.graph)
+        flops = 4.0 * heads * a.m * a.m * 128
+        out.update(m=a.m, heads=heads, ms=ms, tflops=flops / (ms / 1e3) / 1e12)
     elif a.case in ("compress", "restore", "restore_torch", "layout"):
         from . import flash
         t, h, w = torch.meshgrid(torch.arange(21), torch.arange(48), torch.arange(64), indexing="ij")
