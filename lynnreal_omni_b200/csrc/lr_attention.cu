@@ -4,19 +4,25 @@
 // any token stride), fp32 scores and online softmax, bf16 output — the role
 // of the attention backend behind FusedAttention (model/fusion.py:55-57).
 //
-// One CTA per (128-query tile, head, batch); 6 warps:
-//   warp 0     TMA producer: the Q tile once, then K_j and V_j tiles (128 keys
-//              each, 128-byte swizzle) into a 2-stage ring;
-//   warp 1     one thread issues tcgen05.mma.kind::f16 (bf16 in, fp32 TMEM):
-//              S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1} is
-//              computed while softmax reads S_j), then O += P_j V_j as soon as
-//              softmax has written P_j; V is read as an MN-major operand
-//              straight from its TMA tile;
-//   warps 2-5  softmax, one thread per query row (= TMEM lane): running max and
-//              sum in fp32 with exp2, O rescaled in TMEM when the max grows,
-//              P_j written as bf16 to shared memory in the swizzled K-major
-//              layout the MMA reads; at the end O / l -> bf16 -> global.
-// TMEM columns: S buffers at 0 and 128, O at 256 (512 allocated).
+// One CTA per (256 queries = two 128-row tiles A and B, head, batch); 10 warps:
+//   warp 0     TMA producer: both Q tiles once, then K_j and V_j (128 keys each,
+//              128-byte swizzle) into two K and two V slots, K one tile ahead
+//              of V (a K slot frees after both Q K^T, a V slot after both P V);
+//   warp 1     one thread issues tcgen05.mma.kind::f16 (bf16 in, fp32 TMEM) in
+//              the ping-pong order  S_A(0) S_B(0) | O_A+=P_A(j)V_j  S_A(j+1)
+//              O_B+=P_B(j)V_j  S_B(j+1) | ...  so the tensor core works on one
+//              tile while the other tile's softmax runs; P is read from TMEM
+//              (A operand) and V as an MN-major operand from its TMA tile;
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one thread per query
+//              row (= TMEM lane) reads its 128 scores, keeps the running max
+//              and sum in fp32 with exp2 (the max moves only when it grows by
+//              more than 2^8: exact, since O and l share it, and O is rescaled
+//              in TMEM rarely), writes P_j as bf16 pairs over the consumed
+//              score columns, and at the end writes O / l as bf16.
+// TMEM columns: S_A 0-127, S_B 128-255 (P over their first 64 columns),
+// O_A 256-383, O_B 384-511. MMAs of one issuing thread run in order, so
+// S_T(j+1) being ready also means P_T(j) V_j has finished: the softmax of
+// tile j+1 may overwrite P and rescale O without another handshake.
 // Every mbarrier wait is bounded (2 s): on timeout the kernel raises a status
 // bit, lets its own copies and MMAs finish, frees TMEM and returns.
 // No TMA multicast.
@@ -35,19 +41,18 @@ static __device__ unsigned int g_attn_status = 0;
 namespace attn {
 
 constexpr int D = 128;          // head dim
-constexpr int BQ = 128;         // queries per CTA
+constexpr int BQ = 128;         // queries per tile (two tiles per CTA)
 constexpr int BKV = 128;        // keys per tile
 constexpr int ATOM = 128 * 128; // one [128 rows x 64 bf16] swizzle-128B box
 constexpr int TILE = 2 * ATOM;  // [128 rows x 128 bf16]
-constexpr int STAGES = 2;
-constexpr int NUM_THREADS = 192;
-constexpr int SMEM_Q = 0;
-constexpr int SMEM_KV = TILE;                       // stage s: K at +2*TILE*s, V at +TILE
-constexpr int SMEM_P = SMEM_KV + STAGES * 2 * TILE;
-constexpr int SMEM_BAR = SMEM_P + TILE;
+constexpr int NUM_THREADS = 64 + 32 * 8;
+constexpr int SMEM_Q = 0;                 // tile A, then tile B
+constexpr int SMEM_K = 2 * TILE;          // two K slots
+constexpr int SMEM_V = SMEM_K + 2 * TILE; // two V slots
+constexpr int SMEM_BAR = SMEM_V + 2 * TILE;
 constexpr size_t SMEM_BYTES = 1024 + SMEM_BAR + 256;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_O = 256;
+constexpr uint32_t COL_O = 256;           // O_T at COL_O + 128 * T; S_T at 128 * T
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // ------------------------------------------------------------- PTX wrappers
@@ -144,6 +149,16 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D += A B with A read from tensor memory (M lanes x K, two bf16 per column).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -161,6 +176,36 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+// Issue a 32-column TMEM load without waiting; the registers are valid only
+// after tmem_wait_ld64 (which takes them as in/out operands, so no use can be
+// scheduled before the wait).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld64(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]),
+                 "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]),
+                 "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]),
+                 "+r"(a[29]), "+r"(a[30]), "+r"(a[31]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]),
+                 "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]),
+                 "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]), "+r"(b[17]),
+                 "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]), "+r"(b[23]), "+r"(b[24]),
+                 "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31])
+               :
+               : "memory");
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -193,32 +238,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
-  uint64_t* q_full = bars;           // Q landed (1 + tx)
-  uint64_t* kv_full = bars + 1;      // [2] K_j, V_j landed (1 + tx)
-  uint64_t* kv_empty = bars + 3;     // [2] P_j V_j done, stage free (commit)
-  uint64_t* s_full = bars + 5;       // [2] S_j ready (commit)
-  uint64_t* s_free = bars + 7;       // [2] softmax read S_j (4 warps)
-  uint64_t* p_full = bars + 9;       // P_j written, O rescaled (4 warps)
-  uint64_t* o_done = bars + 10;      // P_j V_j done (commit)
-  uint64_t* drain = bars + 11;       // abort-path MMA drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* q_full = bars;           // both Q tiles landed (1 + tx)
+  uint64_t* k_full = bars + 1;       // [2] K_j landed (1 + tx)
+  uint64_t* v_full = bars + 3;       // [2] V_j landed (1 + tx)
+  uint64_t* k_empty = bars + 5;      // [2] both Q K_j^T done (commit)
+  uint64_t* v_empty = bars + 7;      // [2] both P_j V_j done (commit)
+  uint64_t* s_full = bars + 9;       // [tile] S_T(j) ready (commit)
+  uint64_t* p_full = bars + 11;      // [tile] P_T(j) written, O_T rescaled (4 warps)
+  uint64_t* o_done = bars + 13;      // [tile] last P_T V done (commit)
+  uint64_t* drain = bars + 15;       // MMA drain before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, head = blockIdx.y, batch = blockIdx.z;
-  const int q0 = qt * BQ;
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int q0 = blockIdx.x * 2 * BQ;
   const int tiles = (sh.seq_kv + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&kv_full[s]), 1);
-      mbar_init(smem_u32(&kv_empty[s]), 1);
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
       mbar_init(smem_u32(&s_full[s]), 1);
-      mbar_init(smem_u32(&s_free[s]), 4);
+      mbar_init(smem_u32(&p_full[s]), 4);
+      mbar_init(smem_u32(&o_done[s]), 1);
     }
-    mbar_init(smem_u32(p_full), 4);
-    mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -241,39 +288,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
       const int32_t x0 = head * D;
-      uint32_t qb = smem_u32(q_full);
-      mbar_expect_tx(qb, TILE);
-      tma_load_3d(smem_u32(smem + SMEM_Q), &map_q, qb, x0, q0, batch);
-      tma_load_3d(smem_u32(smem + SMEM_Q + ATOM), &map_q, qb, x0 + 64, q0, batch);
-      bool issued[2] = {false, false};
-      uint32_t issued_phase[2] = {0u, 0u};
+      const uint32_t qb = smem_u32(q_full);
+      mbar_expect_tx(qb, 2 * TILE);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_3d(smem_u32(smem + SMEM_Q + t * TILE), &map_q, qb, x0, q0 + t * BQ, batch);
+        tma_load_3d(smem_u32(smem + SMEM_Q + t * TILE + ATOM), &map_q, qb, x0 + 64, q0 + t * BQ, batch);
+      }
+      bool issued[4] = {false, false, false, false};  // k0 k1 v0 v1
+      uint32_t issued_phase[4] = {0u, 0u, 0u, 0u};
       bool ok = true;
-      for (int j = 0; j < tiles && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!wait_bounded(smem_u32(&kv_empty[st]), ph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
+      for (int i = 0; i <= tiles && ok; ++i) {
+        if (i < tiles) {
+          const int st = i & 1;
+          const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+          if (!wait_bounded(smem_u32(&k_empty[st]), ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&k_full[st]);
+          uint8_t* dst = smem + SMEM_K + st * TILE;
+          mbar_expect_tx(fb, TILE);
+          tma_load_3d(smem_u32(dst), &map_k, fb, x0, i * BKV, batch);
+          tma_load_3d(smem_u32(dst + ATOM), &map_k, fb, x0 + 64, i * BKV, batch);
+          issued[st] = true;
+          issued_phase[st] = ph;
         }
-        const uint32_t fb = smem_u32(&kv_full[st]);
-        uint8_t* kdst = smem + SMEM_KV + st * 2 * TILE;
-        mbar_expect_tx(fb, 2 * TILE);
-        tma_load_3d(smem_u32(kdst), &map_k, fb, x0, j * BKV, batch);
-        tma_load_3d(smem_u32(kdst + ATOM), &map_k, fb, x0 + 64, j * BKV, batch);
-        tma_load_3d(smem_u32(kdst + TILE), &map_v, fb, x0, j * BKV, batch);
-        tma_load_3d(smem_u32(kdst + TILE + ATOM), &map_v, fb, x0 + 64, j * BKV, batch);
-        issued[st] = true;
-        issued_phase[st] = ph;
+        if (i >= 1) {
+          const int j = i - 1, st = j & 1;
+          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+          if (!wait_bounded(smem_u32(&v_empty[st]), ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&v_full[st]);
+          uint8_t* dst = smem + SMEM_V + st * TILE;
+          mbar_expect_tx(fb, TILE);
+          tma_load_3d(smem_u32(dst), &map_v, fb, x0, j * BKV, batch);
+          tma_load_3d(smem_u32(dst + ATOM), &map_v, fb, x0 + 64, j * BKV, batch);
+          issued[2 + st] = true;
+          issued_phase[2 + st] = ph;
+        }
       }
       // Let every copy issued by this thread land before the CTA can exit.
       const unsigned long long t0 = globaltimer();
       while (!mbar_try_wait(qb, 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
       }
       if (!ok)
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < 4; ++s)
           if (issued[s]) {
+            const uint32_t fb = smem_u32(s < 2 ? &k_full[s] : &v_full[s - 2]);
             const unsigned long long t1 = globaltimer();
-            while (!mbar_try_wait(smem_u32(&kv_full[s]), issued_phase[s]) && globaltimer() - t1 < kWaitLimitNs / 4) {
+            while (!mbar_try_wait(fb, issued_phase[s]) && globaltimer() - t1 < kWaitLimitNs / 4) {
             }
           }
     }
@@ -283,42 +348,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = wait_bounded(smem_u32(q_full), 0u, abort_flag);
       tc_fence_after();
       const uint32_t qa = smem_u32(smem + SMEM_Q);
-      const uint32_t pa = smem_u32(smem + SMEM_P);
-      for (int j = 0; j <= tiles && ok; ++j) {
-        if (j < tiles) {
-          const int st = j & 1;
-          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-          if (!wait_bounded(smem_u32(&kv_full[st]), ph, abort_flag) ||
-              !wait_bounded(smem_u32(&s_free[st]), ph ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ka = smem_u32(smem + SMEM_KV + st * 2 * TILE);
+      // S_T(j) = Q_T K_j^T into TMEM columns [128 T, 128 T + 128).
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t ka = smem_u32(smem + SMEM_K + (j & 1) * TILE);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (uint32_t)((kk >> 2) * ATOM + (kk & 3) * 32);
-            mma_f16(tmem + (uint32_t)(st * BKV), desc_kmajor(qa + off), desc_kmajor(ka + off), kIdescQK,
-                    kk != 0 ? 1u : 0u);
-          }
-          mma_commit(smem_u32(&s_full[st]));
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * ATOM + (kk & 3) * 32);
+          mma_f16(tmem + (uint32_t)(t * BQ), desc_kmajor(qa + t * TILE + off), desc_kmajor(ka + off), kIdescQK,
+                  kk != 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          const int jp = j - 1, st = jp & 1;
-          if (!wait_bounded(smem_u32(p_full), (uint32_t)jp & 1u, abort_flag)) {
+        mma_commit(smem_u32(&s_full[t]));
+      };
+      // O_T += P_T(j) V_j, P_T from TMEM columns [128 T, 128 T + 64).
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t va = smem_u32(smem + SMEM_V + (j & 1) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          mma_f16_ts(tmem + COL_O + (uint32_t)(t * D), tmem + (uint32_t)(t * BQ + kk * 8),
+                     desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV, (j | kk) != 0 ? 1u : 0u);
+      };
+      if (ok && wait_bounded(smem_u32(&k_full[0]), 0u, abort_flag)) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+        mma_commit(smem_u32(&k_empty[0]));
+      } else {
+        ok = false;
+      }
+      for (int j = 0; j < tiles && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        const bool next = j + 1 < tiles;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!wait_bounded(smem_u32(&p_full[t]), (uint32_t)j & 1u, abort_flag) ||
+              (t == 0 && !wait_bounded(smem_u32(&v_full[st]), ph, abort_flag)) ||
+              (t == 0 && next &&
+               !wait_bounded(smem_u32(&k_full[st ^ 1]), (uint32_t)((j + 1) >> 1) & 1u, abort_flag))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t va = smem_u32(smem + SMEM_KV + st * 2 * TILE + TILE);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint32_t poff = (uint32_t)((kk >> 2) * ATOM + (kk & 3) * 32);
-            mma_f16(tmem + COL_O, desc_kmajor(pa + poff), desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV,
-                    (jp | kk) != 0 ? 1u : 0u);
+          issue_pv(t, j);
+          if (t == 1) mma_commit(smem_u32(&v_empty[st]));
+          if (!next) mma_commit(smem_u32(&o_done[t]));
+          if (next) {
+            issue_qk(t, j + 1);
+            if (t == 1) mma_commit(smem_u32(&k_empty[st ^ 1]));
           }
-          mma_commit(smem_u32(o_done));
-          mma_commit(smem_u32(&kv_empty[st]));
         }
       }
       // Wait for every MMA this thread issued before TMEM can be released.
@@ -329,30 +405,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // -------------------------------------------------------- softmax warps
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    const int t = (warp - 2) >> 2;   // query tile: 0 = A (warps 2-5), 1 = B (warps 6-9)
+    const int quad = warp & 3;       // TMEM lanes [32*quad, 32*quad + 32)
     const int row = quad * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    uint8_t* p_row = smem + SMEM_P + row * 128;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + (uint32_t)(t * BQ);
+    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(t * D);
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < tiles; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(smem_u32(&s_full[sb]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
+      // S_T(j) ready; with in-order MMAs this also means P_T(j-1) V_{j-1} is done.
+      if (!warp_wait(smem_u32(&s_full[t]), (uint32_t)j & 1u, abort_flag, lane)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float s[BKV];
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32_nowait(s_col, ra);
+        tmem_ld32_nowait(s_col + 32u, rb);
+        tmem_wait_ld64(ra, rb);
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + (uint32_t)(sb * BKV + c * 32), r);
+        for (int e = 0; e < 32; ++e) {
+          s[e] = __uint_as_float(ra[e]);
+          s[32 + e] = __uint_as_float(rb[e]);
+        }
+        tmem_ld32_nowait(s_col + 64u, ra);
+        tmem_ld32_nowait(s_col + 96u, rb);
+        tmem_wait_ld64(ra, rb);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
+        for (int e = 0; e < 32; ++e) {
+          s[64 + e] = __uint_as_float(ra[e]);
+          s[96 + e] = __uint_as_float(rb[e]);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
       const int valid = sh.seq_kv - j * BKV;
       if (valid < BKV) {
 #pragma unroll
@@ -367,70 +454,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mx2 = fmaxf(mx2, s[e + 2]);
         mx3 = fmaxf(mx3, s[e + 3]);
       }
-      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sh.scale_log2);
-      const float alpha = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
-      const float neg_m = -m_new;
+      const float tile_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sh.scale_log2;
+      // Move the reference max only when it grows by more than 2^8: p <= 256,
+      // no overflow, and O is rescaled rarely (exact: O and l share it).
+      const bool move = tile_max > m_run + 8.0f;
+      const float m_use = move ? tile_max : m_run;
+      const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on the first tile
+      const float neg_m = -m_use;
       float l0 = 0.0f, l1 = 0.0f;
-      uint32_t pk[BKV / 2];
 #pragma unroll
-      for (int e = 0; e < BKV; e += 2) {
-        const float p0 = ex2(fmaf(s[e], sh.scale_log2, neg_m));
-        const float p1 = ex2(fmaf(s[e + 1], sh.scale_log2, neg_m));
-        l0 += p0;
-        l1 += p1;
-        pk[e / 2] = cvt2(p0, p1);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const float p0 = ex2(fmaf(s[64 * h + e], sh.scale_log2, neg_m));
+          const float p1 = ex2(fmaf(s[64 * h + e + 1], sh.scale_log2, neg_m));
+          l0 += p0;
+          l1 += p1;
+          pk[e / 2] = cvt2(p0, p1);
+        }
+        tmem_st32(s_col + (uint32_t)(h * 32), pk);  // P over the consumed score columns
       }
       l_run = fmaf(l_run, alpha, l0 + l1);
-      m_run = m_new;
-      if (j >= 1) {
-        // P_{j-1} V_{j-1} must be done: it reads the P buffer and writes O.
-        if (!warp_wait(smem_u32(o_done), (uint32_t)(j - 1) & 1u, abort_flag, lane)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.0f)) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            const uint32_t ta = lane_base + COL_O + (uint32_t)(c * 32);
-            tmem_ld32(ta, r);
+      m_run = m_use;
+      // O_T rescale (after the scores are consumed, to keep registers free);
+      // P_T(j) V_j cannot start before the p_full arrive below.
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t oa[32], ob[32];
+          tmem_ld32_nowait(o_col + (uint32_t)(c * 64), oa);
+          tmem_ld32_nowait(o_col + (uint32_t)(c * 64 + 32), ob);
+          tmem_wait_ld64(oa, ob);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st32(ta, r);
+          for (int e = 0; e < 32; ++e) {
+            oa[e] = __float_as_uint(__uint_as_float(oa[e]) * alpha);
+            ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
           }
-          tmem_st_wait();
+          tmem_st32(o_col + (uint32_t)(c * 64), oa);
+          tmem_st32(o_col + (uint32_t)(c * 64 + 32), ob);
         }
       }
-      // P row -> shared memory, K-major with 128-byte swizzle: key chunk c
-      // (8 keys, 16 bytes) of row r sits at atom c/8, 16-byte slot (c%8) ^ (r%8).
-#pragma unroll
-      for (int c = 0; c < BKV / 8; ++c) {
-        uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(p_row + (c >> 3) * ATOM + (((c & 7) ^ (row & 7)) << 4)) = v;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(p_full));
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
     }
-    if (ok && warp_wait(smem_u32(o_done), (uint32_t)(tiles - 1) & 1u, abort_flag, lane)) {
+    if (ok && warp_wait(smem_u32(&o_done[t]), 0u, abort_flag, lane)) {
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
-      const int qrow = q0 + row;
+      const int qrow = q0 + t * BQ + row;
       __nv_bfloat16* dst = out + ((int64_t)batch * sh.seq_q + qrow) * sh.out_ts + (int64_t)head * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + COL_O + (uint32_t)(c * 32), r);
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t oa[32], ob[32];
+        tmem_ld32_nowait(o_col + (uint32_t)(c * 64), oa);
+        tmem_ld32_nowait(o_col + (uint32_t)(c * 64 + 32), ob);
+        tmem_wait_ld64(oa, ob);
         if (qrow < sh.seq_q) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[8 * q + e]) * inv_l;
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(oa[8 * q + e]) * inv_l;
             d4[q] = pack8(f);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(ob[8 * q + e]) * inv_l;
+            d4[4 + q] = pack8(f);
           }
         }
       }
@@ -532,7 +625,7 @@ extern "C" int lr_attention_bf16(const void* q, int64_t q_token_stride, const vo
   sh.heads = (int)heads;
   sh.out_ts = out_token_stride;
   sh.scale_log2 = (float)((double)scale * 1.4426950408889634);
-  const dim3 grid((unsigned)((seq_q + attn::BQ - 1) / attn::BQ), (unsigned)heads, (unsigned)batch);
+  const dim3 grid((unsigned)((seq_q + 2 * attn::BQ - 1) / (2 * attn::BQ)), (unsigned)heads, (unsigned)batch);
   attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       mq, mk, mv, sh, static_cast<__nv_bfloat16*>(out));
   return launch_status("attention");
