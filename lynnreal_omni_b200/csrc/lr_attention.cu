@@ -34,6 +34,12 @@
 #include "lr_common.cuh"
 #include "lr_host.h"
 
+// Exponentials evaluated on the FMA pipe instead of the MUFU unit: every
+// LR_ATTN_EMU-th pair of a full key tile (0: none). Tuning knob.
+#ifndef LR_ATTN_EMU
+#define LR_ATTN_EMU 4
+#endif
+
 namespace lr {
 
 static __device__ unsigned int g_attn_status = 0;
@@ -223,6 +229,43 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for a pair, on the FMA pipe: x = n + f with n = round(x) (add and
+// subtract 1.5 * 2^23) and f in [-1/2, 1/2]; 2^f by a cubic fitted to 2^f on
+// that interval (relative error below 7.5e-5, far under the bf16 rounding of
+// P); 2^n by adding n to the exponent field. x is clamped to >= -125 so the
+// result stays a normal float (2^-125 is negligible against a row sum >= 1).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kMagic, kMagic));
+  const float2 n = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);  // exact
+  float2 p = __ffma2_rn(f, make_float2(0.0551716685f, 0.0551716685f), make_float2(0.2426111400f, 0.2426111400f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// P for 64 consecutive scores of a row: p = 2^(s * scale_log2 - m), stored as
+// bf16 pairs into `pk`; the pair sums accumulate into lsum (even, odd keys).
+template <int EMU>
+__device__ __forceinline__ void softmax_half(const float* s, float2 sc2, float2 nm2, float2& lsum,
+                                             uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    const float2 x = __ffma2_rn(make_float2(s[2 * q], s[2 * q + 1]), sc2, nm2);
+    float2 p;
+    if (EMU > 0 && (q % EMU) == EMU - 1)
+      p = exp2_poly2(x);
+    else
+      p = make_float2(ex2(x.x), ex2(x.y));
+    lsum = __fadd2_rn(lsum, p);
+    pk[q] = cvt2(p.x, p.y);
+  }
 }
 
 struct Shape {
@@ -461,20 +504,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = move ? tile_max : m_run;
       const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on the first tile
       const float neg_m = -m_use;
-      float l0 = 0.0f, l1 = 0.0f;
+      const float2 sc2 = make_float2(sh.scale_log2, sh.scale_log2);
+      const float2 nm2 = make_float2(neg_m, neg_m);
+      float2 lsum = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          const float p0 = ex2(fmaf(s[64 * h + e], sh.scale_log2, neg_m));
-          const float p1 = ex2(fmaf(s[64 * h + e + 1], sh.scale_log2, neg_m));
-          l0 += p0;
-          l1 += p1;
-          pk[e / 2] = cvt2(p0, p1);
-        }
+        if (valid >= BKV)
+          softmax_half<LR_ATTN_EMU>(s + 64 * h, sc2, nm2, lsum, pk);
+        else  // masked keys need an exact 0: MUFU only
+          softmax_half<0>(s + 64 * h, sc2, nm2, lsum, pk);
         tmem_st32(s_col + (uint32_t)(h * 32), pk);  // P over the consumed score columns
       }
+      const float l0 = lsum.x, l1 = lsum.y;
       l_run = fmaf(l_run, alpha, l0 + l1);
       m_run = m_use;
       // O_T rescale (after the scores are consumed, to keep registers free);
