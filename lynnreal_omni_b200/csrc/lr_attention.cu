@@ -4,7 +4,7 @@
 // any token stride), fp32 scores and online softmax, bf16 output — the role
 // of the attention backend behind FusedAttention (model/fusion.py:55-57).
 //
-// One CTA per (256 queries = two 128-row tiles A and B, head, batch); 10 warps:
+// One CTA per (256 queries = two 128-row tiles A and B, head, batch); 18 warps:
 //   warp 0     TMA producer: both Q tiles once, then K_j and V_j (128 keys each,
 //              128-byte swizzle) into two K and two V slots, K one tile ahead
 //              of V (a K slot frees after both Q K^T, a V slot after both P V);
@@ -13,8 +13,11 @@
 //              O_B+=P_B(j)V_j  S_B(j+1) | ...  so the tensor core works on one
 //              tile while the other tile's softmax runs; P is read from TMEM
 //              (A operand) and V as an MN-major operand from its TMA tile;
-//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one thread per query
-//              row (= TMEM lane) reads its 128 scores, keeps the running max
+//   warps 2-9  softmax of tile A, warps 10-17 of tile B: two warps per TMEM
+//              lane quadrant, each thread owning one query row (= TMEM lane)
+//              and 64 of its 128 scores per tile; the two halves of a row
+//              exchange maxima and, at the end, sums through shared memory
+//              (mbarriers, bounded waits). Each keeps the running max
 //              and sum in fp32 with exp2 (the max moves only when it grows by
 //              more than 2^8: exact, since O and l share it, and O is rescaled
 //              in TMEM rarely), writes P_j as bf16 pairs over the consumed
@@ -51,12 +54,15 @@ constexpr int BQ = 128;         // queries per tile (two tiles per CTA)
 constexpr int BKV = 128;        // keys per tile
 constexpr int ATOM = 128 * 128; // one [128 rows x 64 bf16] swizzle-128B box
 constexpr int TILE = 2 * ATOM;  // [128 rows x 128 bf16]
-constexpr int NUM_THREADS = 64 + 32 * 8;
+constexpr int SOFTMAX_WARPS = 16;  // per tile: two warps per TMEM lane quadrant (64 keys each)
+constexpr int NUM_THREADS = 64 + 32 * SOFTMAX_WARPS;
 constexpr int SMEM_Q = 0;                 // tile A, then tile B
 constexpr int SMEM_K = 2 * TILE;          // two K slots
 constexpr int SMEM_V = SMEM_K + 2 * TILE; // two V slots
-constexpr int SMEM_BAR = SMEM_V + 2 * TILE;
-constexpr size_t SMEM_BYTES = 1024 + SMEM_BAR + 256;
+constexpr int SMEM_RED = SMEM_V + 2 * TILE;  // [tile][parity][half][row] fp32
+constexpr int SMEM_BAR = SMEM_RED + 2 * 2 * 2 * BQ * 4;
+constexpr int BAR_BYTES = 512;  // 32 mbarriers (256 B) + TMEM slot + abort flag
+constexpr size_t SMEM_BYTES = 1024 + SMEM_BAR + BAR_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_O = 256;           // O_T at COL_O + 128 * T; S_T at 128 * T
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
@@ -287,10 +293,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* k_empty = bars + 5;      // [2] both Q K_j^T done (commit)
   uint64_t* v_empty = bars + 7;      // [2] both P_j V_j done (commit)
   uint64_t* s_full = bars + 9;       // [tile] S_T(j) ready (commit)
-  uint64_t* p_full = bars + 11;      // [tile] P_T(j) written, O_T rescaled (4 warps)
+  uint64_t* p_full = bars + 11;      // [tile] P_T(j) written, O_T rescaled (8 warps)
   uint64_t* o_done = bars + 13;      // [tile] last P_T V done (commit)
   uint64_t* drain = bars + 15;       // MMA drain before TMEM is freed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* red_bar = bars + 16;     // [tile][quadrant][parity] exchange between a row's two halves (2 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);  // within BAR_BYTES
+  static_assert(32 * 8 + 8 <= BAR_BYTES, "barrier region");
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -306,10 +314,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(smem_u32(&k_empty[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
       mbar_init(smem_u32(&s_full[s]), 1);
-      mbar_init(smem_u32(&p_full[s]), 4);
+      mbar_init(smem_u32(&p_full[s]), SOFTMAX_WARPS / 2);
       mbar_init(smem_u32(&o_done[s]), 1);
     }
     mbar_init(smem_u32(drain), 1);
+    for (int b = 0; b < 16; ++b) mbar_init(smem_u32(&red_bar[b]), 2);
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&map_q);
@@ -448,125 +457,138 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // -------------------------------------------------------- softmax warps
-    const int t = (warp - 2) >> 2;   // query tile: 0 = A (warps 2-5), 1 = B (warps 6-9)
-    const int quad = warp & 3;       // TMEM lanes [32*quad, 32*quad + 32)
+    const int idx = warp - 2;
+    const int t = idx >> 3;              // query tile: 0 = A (warps 2-9), 1 = B (warps 10-17)
+    const int half = (idx >> 2) & 1;     // keys / output columns [64 half, 64 half + 64)
+    const int quad = warp & 3;           // TMEM lanes [32 quad, 32 quad + 32)
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t s_col = tmem + lane_off + (uint32_t)(t * BQ);
-    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(t * D);
+    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(t * D + half * 64);
+    float* red = reinterpret_cast<float*>(smem + SMEM_RED) + t * 2 * 2 * BQ;  // [parity][half][row]
+    uint64_t* xbar = red_bar + t * 8 + quad * 2;                               // [parity]
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < tiles; ++j) {
-      // S_T(j) ready; with in-order MMAs this also means P_T(j-1) V_{j-1} is done.
-      if (!warp_wait(smem_u32(&s_full[t]), (uint32_t)j & 1u, abort_flag, lane)) {
+      const int par = j & 1;
+      // S_T(j) ready; this also means P_T(j-1) V_{j-1} is done (same commit).
+      if (!warp_wait(smem_u32(&s_full[t]), (uint32_t)par, abort_flag, lane)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[BKV];
+      float s[64];
       {
         uint32_t ra[32], rb[32];
-        tmem_ld32_nowait(s_col, ra);
-        tmem_ld32_nowait(s_col + 32u, rb);
+        tmem_ld32_nowait(s_col + (uint32_t)(half * 64), ra);
+        tmem_ld32_nowait(s_col + (uint32_t)(half * 64 + 32), rb);
         tmem_wait_ld64(ra, rb);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           s[e] = __uint_as_float(ra[e]);
           s[32 + e] = __uint_as_float(rb[e]);
         }
-        tmem_ld32_nowait(s_col + 64u, ra);
-        tmem_ld32_nowait(s_col + 96u, rb);
-        tmem_wait_ld64(ra, rb);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          s[64 + e] = __uint_as_float(ra[e]);
-          s[96 + e] = __uint_as_float(rb[e]);
-        }
       }
-      const int valid = sh.seq_kv - j * BKV;
-      if (valid < BKV) {
+      const int valid = sh.seq_kv - j * BKV - half * 64;
+      if (valid < 64) {
 #pragma unroll
-        for (int e = 0; e < BKV; ++e)
+        for (int e = 0; e < 64; ++e)
           if (e >= valid) s[e] = -INFINITY;
       }
       float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-      for (int e = 4; e < BKV; e += 4) {
+      for (int e = 4; e < 64; e += 4) {
         mx0 = fmaxf(mx0, s[e]);
         mx1 = fmaxf(mx1, s[e + 1]);
         mx2 = fmaxf(mx2, s[e + 2]);
         mx3 = fmaxf(mx3, s[e + 3]);
       }
-      const float tile_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sh.scale_log2;
+      // Row max over both halves: publish, then wait (bounded) for the partner
+      // warp's value of this tile parity. A slot is rewritten two tiles later,
+      // after the partner has read it (it must arrive again in between).
+      red[(par * 2 + half) * BQ + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&xbar[par]));
+      if (!warp_wait(smem_u32(&xbar[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
+      const float tile_max =
+          fmaxf(red[(par * 2) * BQ + row], red[(par * 2 + 1) * BQ + row]) * sh.scale_log2;
       // Move the reference max only when it grows by more than 2^8: p <= 256,
-      // no overflow, and O is rescaled rarely (exact: O and l share it).
+      // no overflow, and O is rescaled rarely (exact: O and l share it). Both
+      // halves of a row decide identically.
       const bool move = tile_max > m_run + 8.0f;
       const float m_use = move ? tile_max : m_run;
       const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on the first tile
-      const float neg_m = -m_use;
       const float2 sc2 = make_float2(sh.scale_log2, sh.scale_log2);
-      const float2 nm2 = make_float2(neg_m, neg_m);
+      const float2 nm2 = make_float2(-m_use, -m_use);
       float2 lsum = make_float2(0.0f, 0.0f);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      {
         uint32_t pk[32];
-        if (valid >= BKV)
-          softmax_half<LR_ATTN_EMU>(s + 64 * h, sc2, nm2, lsum, pk);
+        if (valid >= 64)
+          softmax_half<LR_ATTN_EMU>(s, sc2, nm2, lsum, pk);
         else  // masked keys need an exact 0: MUFU only
-          softmax_half<0>(s + 64 * h, sc2, nm2, lsum, pk);
-        tmem_st32(s_col + (uint32_t)(h * 32), pk);  // P over the consumed score columns
+          softmax_half<0>(s, sc2, nm2, lsum, pk);
+        tmem_st32(s_col + (uint32_t)(half * 32), pk);  // P over the consumed score columns
       }
-      const float l0 = lsum.x, l1 = lsum.y;
-      l_run = fmaf(l_run, alpha, l0 + l1);
+      l_run = fmaf(l_run, alpha, lsum.x + lsum.y);
       m_run = m_use;
-      // O_T rescale (after the scores are consumed, to keep registers free);
-      // P_T(j) V_j cannot start before the p_full arrive below.
+      // O_T rescale of this half's 64 columns; P_T(j) V_j cannot start before
+      // the p_full arrive below.
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t oa[32], ob[32];
-          tmem_ld32_nowait(o_col + (uint32_t)(c * 64), oa);
-          tmem_ld32_nowait(o_col + (uint32_t)(c * 64 + 32), ob);
-          tmem_wait_ld64(oa, ob);
+        uint32_t oa[32], ob[32];
+        tmem_ld32_nowait(o_col, oa);
+        tmem_ld32_nowait(o_col + 32u, ob);
+        tmem_wait_ld64(oa, ob);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            oa[e] = __float_as_uint(__uint_as_float(oa[e]) * alpha);
-            ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
-          }
-          tmem_st32(o_col + (uint32_t)(c * 64), oa);
-          tmem_st32(o_col + (uint32_t)(c * 64 + 32), ob);
+        for (int e = 0; e < 32; ++e) {
+          oa[e] = __float_as_uint(__uint_as_float(oa[e]) * alpha);
+          ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
         }
+        tmem_st32(o_col, oa);
+        tmem_st32(o_col + 32u, ob);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
     }
+    // Each half holds the row sum over its keys against the same max; the
+    // exchange uses the parity the last tile did not (read by both already).
+    float l_other = 0.0f;
+    if (ok) {
+      const int pe = tiles & 1;
+      red[(pe * 2 + half) * BQ + row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&xbar[pe]));
+      ok = warp_wait(smem_u32(&xbar[pe]), (uint32_t)(tiles >> 1) & 1u, abort_flag, lane);
+      if (ok) l_other = red[(pe * 2 + 1 - half) * BQ + row];
+    }
     if (ok && warp_wait(smem_u32(&o_done[t]), 0u, abort_flag, lane)) {
       tc_fence_after();
-      const float inv_l = 1.0f / l_run;
+      const float inv_l = 1.0f / (half == 0 ? l_run + l_other : l_other + l_run);
       const int qrow = q0 + t * BQ + row;
-      __nv_bfloat16* dst = out + ((int64_t)batch * sh.seq_q + qrow) * sh.out_ts + (int64_t)head * D;
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t oa[32], ob[32];
-        tmem_ld32_nowait(o_col + (uint32_t)(c * 64), oa);
-        tmem_ld32_nowait(o_col + (uint32_t)(c * 64 + 32), ob);
-        tmem_wait_ld64(oa, ob);
-        if (qrow < sh.seq_q) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
+      uint32_t oa[32], ob[32];
+      tmem_ld32_nowait(o_col, oa);
+      tmem_ld32_nowait(o_col + 32u, ob);
+      tmem_wait_ld64(oa, ob);
+      if (qrow < sh.seq_q) {
+        uint4* d4 = reinterpret_cast<uint4*>(out + ((int64_t)batch * sh.seq_q + qrow) * sh.out_ts +
+                                             (int64_t)head * D + half * 64);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float f[8];
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(oa[8 * q + e]) * inv_l;
-            d4[q] = pack8(f);
-          }
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(oa[8 * q + e]) * inv_l;
+          d4[q] = pack8(f);
+        }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float f[8];
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(ob[8 * q + e]) * inv_l;
-            d4[4 + q] = pack8(f);
-          }
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(ob[8 * q + e]) * inv_l;
+          d4[4 + q] = pack8(f);
         }
       }
     }
