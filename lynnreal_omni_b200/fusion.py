@@ -13,10 +13,11 @@ Differences, all deliberate:
     GPU instead of only on capability 9;
   * the Q/K RMSNorm+RoPE has one fixed reduction order, so the ``ordered_qk``
     option is accepted and has no effect;
-  * the attention core (out of the projection path's scope) is
-    ``torch.nn.functional.scaled_dot_product_attention`` unless an
+  * the attention core is this package's tcgen05 kernel
+    (``attention.attention_bshd``: bf16, head_dim 128, no mask) unless an
     ``attention_fn(q, k, v, attn_mask)`` taking [B, S, H, D] tensors is given
-    (e.g. diffusers' ``dispatch_attention_fn``).
+    (``sdpa_bshd`` for torch's SDPA, e.g. when a mask is needed, or diffusers'
+    ``dispatch_attention_fn``).
 """
 from __future__ import annotations
 
@@ -27,6 +28,7 @@ import torch
 import torch.nn.functional as F
 
 from . import kernels as k
+from .attention import attention_bshd
 
 
 def sdpa_bshd(query, key, value, attn_mask=None):
@@ -44,7 +46,7 @@ class FusedAttention:
         self.ordered_qk = ordered_qk
         self._attention_backend = getattr(original, "_attention_backend", None)
         self._parallel_config = getattr(original, "_parallel_config", None)
-        self.attention_fn = attention_fn or sdpa_bshd
+        self.attention_fn = attention_fn or attention_bshd
 
     def __call__(self, attn, hidden_states, rotary_emb=None, attention_mask=None):
         if rotary_emb is None or rotary_emb[0].ndim != 2:

@@ -23,6 +23,7 @@ from torch import nn
 
 from oracle import w8a8_oracle as O
 from lynnreal_omni_b200 import _lib, fusion, kernels as K, workloads
+from lynnreal_omni_b200.attention import attention_bshd
 from lynnreal_omni_b200.int8 import Int8Linear
 
 pytestmark = pytest.mark.gpu
@@ -180,9 +181,27 @@ def _packed(n, k, gen):
     return p.weight, p.scale, p.bias
 
 
+def manual_block(block, x, temb, idx, rot, hidden, heads):
+    """The fused block's kernels called one by one in the reference's order
+    (model/fusion.py:61-98)."""
+    lin = block.adaln_proj.linear
+    table = lin(F.silu(temb).to(lin.weight.dtype)).view(-1, 6 * hidden)
+    q8, sc = K._rms_adaln_quant_int8(x, block.norm1, table, idx, 0, 1)
+    qkv = block.attn.to_qkv.forward_quantized(q8, sc, x.shape[:-1])
+    q, k, v = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+    qo, ko = K.qk_norm_rope(q, k, block.attn.norm_q, block.attn.norm_k, rot)
+    att = attention_bshd(qo, ko, v)
+    ao = block.attn.to_out[0](att.flatten(2, 3).type_as(qo))
+    h, q8, sc = K.residual_rms_quant(x, ao, block.norm2, table, idx)
+    proj = block.ff.net[0].proj.forward_quantized(q8, sc, h.shape[:-1])
+    q8, sc = K._swiglu_quant_int8(proj)
+    out = block.ff.net[2].forward_quantized(q8, sc, proj.shape[:-1])
+    return K._gated_residual(h, out, table, idx, 5)
+
+
 def test_fused_block_runs_the_reference_sequence():
     gen = torch.Generator().manual_seed(61)
-    hidden, heads, inner, s = 512, 4, 768, 37
+    hidden, heads, inner, s = 512, 4, 768, 300
     block = _Block(hidden, heads, inner, gen).to(DEV)
     report = fusion.enable_fusion(SimpleNamespace(transformer_blocks=[block]), fused_quant=True)
     assert report["residual_ffn_norm_fused"] and report["activation_quantization_fused"]
@@ -193,18 +212,23 @@ def test_fused_block_runs_the_reference_sequence():
     rot = (phase.cos(), phase.sin())
     got = block.forward(x, temb, idx, rot)
 
-    # the same kernels, called one by one in the reference's order
-    table = block.adaln_linear(F.silu(temb).to(torch.bfloat16)).view(-1, 6 * hidden)
-    q8, sc = K._rms_adaln_quant_int8(x, block.norm1, table, idx, 0, 1)
-    qkv = block.attn.to_qkv.forward_quantized(q8, sc, x.shape[:-1])
-    q, k, v = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
-    qo, ko = K.qk_norm_rope(q, k, block.attn.norm_q, block.attn.norm_k, rot)
-    att = fusion.sdpa_bshd(qo, ko, v)
-    ao = block.attn.to_out[0](att.flatten(2, 3).type_as(qo))
-    h, q8, sc = K.residual_rms_quant(x, ao, block.norm2, table, idx)
-    proj = block.ff.net[0].proj.forward_quantized(q8, sc, h.shape[:-1])
-    q8, sc = K._swiglu_quant_int8(proj)
-    out = block.ff.net[2].forward_quantized(q8, sc, proj.shape[:-1])
-    expect = K._gated_residual(h, out, table, idx, 5)
+    expect = manual_block(block, x, temb, idx, rot, hidden, heads)
     assert torch.equal(got, expect)
+    assert _lib.device_status(clear=True) == 0
+
+
+def test_flash_block_module_through_enable_fusion():
+    """lynnreal_omni_b200.flash_block.FlashH3Block (released Flash block layout,
+    reduced widths here) runs through enable_fusion and equals the manual
+    kernel sequence."""
+    from lynnreal_omni_b200 import flash_block as FB
+    hidden, heads = 512, 4
+    block = FB.FlashH3Block(seed=3, device=DEV, hidden=hidden, heads=heads, ffn_inner=640).eval()
+    fusion.enable_fusion(SimpleNamespace(transformer_blocks=[block]), fused_quant=True)
+    x, temb, idx, rot = FB.make_inputs(257, seed=4, device=DEV, hidden=hidden)
+    with torch.no_grad():
+        got = block.forward(x, temb, idx, rot)
+        expect = manual_block(block, x, temb, idx, rot, hidden, heads)
+    assert torch.equal(got, expect)
+    assert torch.isfinite(got.float()).all()
     assert _lib.device_status(clear=True) == 0
