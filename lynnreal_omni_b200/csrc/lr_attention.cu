@@ -4,28 +4,28 @@
 // any token stride), fp32 scores and online softmax, bf16 output — the role
 // of the attention backend behind FusedAttention (model/fusion.py:55-57).
 //
-// One CTA per (256 queries = two 128-row tiles A and B, head, batch); 18 warps:
-//   warp 0     TMA producer: both Q tiles once, then K_j and V_j (128 keys each,
-//              128-byte swizzle) into two K and two V slots, K one tile ahead
-//              of V (a K slot frees after both Q K^T, a V slot after both P V);
-//   warp 1     one thread issues tcgen05.mma.kind::f16 (bf16 in, fp32 TMEM) in
-//              the ping-pong order  S_A(0) S_B(0) | O_A+=P_A(j)V_j  S_A(j+1)
-//              O_B+=P_B(j)V_j  S_B(j+1) | ...  so the tensor core works on one
-//              tile while the other tile's softmax runs; P is read from TMEM
-//              (A operand) and V as an MN-major operand from its TMA tile;
-//   warps 2-9  softmax of tile A, warps 10-17 of tile B: two warps per TMEM
-//              lane quadrant, each thread owning one query row (= TMEM lane)
-//              and 64 of its 128 scores per tile; the two halves of a row
-//              exchange maxima and, at the end, sums through shared memory
-//              (mbarriers, bounded waits). Each keeps the running max
-//              and sum in fp32 with exp2 (the max moves only when it grows by
-//              more than 2^8: exact, since O and l share it, and O is rescaled
-//              in TMEM rarely), writes P_j as bf16 pairs over the consumed
-//              score columns, and at the end writes O / l as bf16.
-// TMEM columns: S_A 0-127, S_B 128-255 (P over their first 64 columns),
-// O_A 256-383, O_B 384-511. MMAs of one issuing thread run in order, so
-// S_T(j+1) being ready also means P_T(j) V_j has finished: the softmax of
-// tile j+1 may overwrite P and rescale O without another handshake.
+// One CTA per (128 queries, head, batch); 10 warps:
+//   warp 0     TMA producer: the Q tile once, then 128-key K_j and V_j tiles
+//              (128-byte swizzle) into three K and two V slots, K two tiles
+//              ahead of V (a K slot frees after Q K^T, a V slot after P V);
+//   warp 1     one thread issues tcgen05.mma.kind::f16 (bf16 in, fp32 TMEM):
+//              S(0), S(1), then per key tile j: O += P(j) V_j followed by
+//              S(j+2) = Q K_{j+2}^T into the score buffer P(j) occupied (MMAs
+//              of one thread run in order). Scores are double-buffered, so
+//              S(j+1) is computed while the softmax of tile j runs and the
+//              softmax never waits on its own tile's MMAs. P is read from
+//              TMEM (A operand), V as an MN-major operand from its TMA tile;
+//   warps 2-9  softmax: two warps per TMEM lane quadrant, each thread owning a
+//              query row (= TMEM lane) and one 64-key half of every score
+//              tile; the halves exchange row maxima (and, at the end, sums)
+//              through shared memory with bounded mbarrier waits. Running max
+//              and sum in fp32 with exp2 (a quarter of each full tile's
+//              exponentials on the FMA pipe); the max moves only when it grows
+//              by more than 2^8 (exact, since O and l share it), so O is
+//              rescaled in TMEM rarely, after its previous P V has finished;
+//              P(j) is written as bf16 pairs over consumed score columns; at
+//              the end O / l -> bf16 -> global.
+// TMEM columns: score buffers at 0 and 128, O at 256 (512 allocated).
 // Every mbarrier wait is bounded (2 s): on timeout the kernel raises a status
 // bit, lets its own copies and MMAs finish, frees TMEM and returns.
 // No TMA multicast.
@@ -49,22 +49,24 @@ static __device__ unsigned int g_attn_status = 0;
 
 namespace attn {
 
-constexpr int D = 128;          // head dim
-constexpr int BQ = 128;         // queries per tile (two tiles per CTA)
-constexpr int BKV = 128;        // keys per tile
-constexpr int ATOM = 128 * 128; // one [128 rows x 64 bf16] swizzle-128B box
-constexpr int TILE = 2 * ATOM;  // [128 rows x 128 bf16]
-constexpr int SOFTMAX_WARPS = 16;  // per tile: two warps per TMEM lane quadrant (64 keys each)
+constexpr int D = 128;             // head dim
+constexpr int BQ = 128;            // queries per CTA
+constexpr int BKV = 128;           // keys per score tile
+constexpr int ATOM = 128 * 128;    // [128 rows x 64 bf16] swizzle-128B box
+constexpr int TILE = 2 * ATOM;     // [128 rows x 128 bf16]
+constexpr int K_SLOTS = 3;
+constexpr int V_SLOTS = 2;
+constexpr int SOFTMAX_WARPS = 8;   // two per TMEM lane quadrant (64 keys each)
 constexpr int NUM_THREADS = 64 + 32 * SOFTMAX_WARPS;
-constexpr int SMEM_Q = 0;                 // tile A, then tile B
-constexpr int SMEM_K = 2 * TILE;          // two K slots
-constexpr int SMEM_V = SMEM_K + 2 * TILE; // two V slots
-constexpr int SMEM_RED = SMEM_V + 2 * TILE;  // [tile][parity][half][row] fp32
-constexpr int SMEM_BAR = SMEM_RED + 2 * 2 * 2 * BQ * 4;
-constexpr int BAR_BYTES = 512;  // 32 mbarriers (256 B) + TMEM slot + abort flag
+constexpr int SMEM_Q = 0;
+constexpr int SMEM_K = TILE;                        // K slots
+constexpr int SMEM_V = SMEM_K + K_SLOTS * TILE;     // V slots
+constexpr int SMEM_RED = SMEM_V + V_SLOTS * TILE;   // [parity][half][row] fp32
+constexpr int SMEM_BAR = SMEM_RED + 2 * 2 * BQ * 4;
+constexpr int BAR_BYTES = 512;
 constexpr size_t SMEM_BYTES = 1024 + SMEM_BAR + BAR_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_O = 256;           // O_T at COL_O + 128 * T; S_T at 128 * T
+constexpr uint32_t COL_O = 256;  // score buffers at 0 and 128, O at 256
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // ------------------------------------------------------------- PTX wrappers
@@ -139,8 +141,8 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
 }
 // MN-major operand, 128-byte swizzle: 64 contiguous MN elements (128 bytes)
 // per row, K rows 128 bytes apart; the leading byte offset steps between
-// 64-element MN blocks (the two TMA boxes of a tile, ATOM bytes apart), the
-// stride byte offset between 8-row K groups (1024 bytes).
+// 64-element MN blocks (the two TMA boxes of a V tile, ATOM bytes apart),
+// the stride byte offset between 8-row K groups (1024 bytes).
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(ATOM >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) |
          ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
@@ -287,38 +289,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
-  uint64_t* q_full = bars;           // both Q tiles landed (1 + tx)
-  uint64_t* k_full = bars + 1;       // [2] K_j landed (1 + tx)
-  uint64_t* v_full = bars + 3;       // [2] V_j landed (1 + tx)
-  uint64_t* k_empty = bars + 5;      // [2] both Q K_j^T done (commit)
-  uint64_t* v_empty = bars + 7;      // [2] both P_j V_j done (commit)
-  uint64_t* s_full = bars + 9;       // [tile] S_T(j) ready (commit)
-  uint64_t* p_full = bars + 11;      // [tile] P_T(j) written, O_T rescaled (8 warps)
-  uint64_t* o_done = bars + 13;      // [tile] last P_T V done (commit)
-  uint64_t* drain = bars + 15;       // MMA drain before TMEM is freed
-  uint64_t* red_bar = bars + 16;     // [tile][quadrant][parity] exchange between a row's two halves (2 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);  // within BAR_BYTES
-  static_assert(32 * 8 + 8 <= BAR_BYTES, "barrier region");
+  uint64_t* q_full = bars;           // Q landed (1 + tx)
+  uint64_t* k_full = bars + 1;       // [3] K_j landed (1 + tx)
+  uint64_t* k_empty = bars + 4;      // [3] Q K_j^T done (commit)
+  uint64_t* v_full = bars + 7;       // [2] V_j landed (1 + tx)
+  uint64_t* v_empty = bars + 9;      // [2] P_j V_j done (commit)
+  uint64_t* s_full = bars + 11;      // [buffer] S(j) ready (commit)
+  // p_full alternates by tile parity: the softmax may finish tile j + 1 before
+  // the MMA thread has consumed tile j, and a barrier must never run two
+  // phases ahead of its waiter.
+  uint64_t* p_full = bars + 13;      // [j & 1] P(j) written, O rescaled (8 warps)
+  uint64_t* pv_done = bars + 15;     // P(j) V_j done (commit, every j)
+  uint64_t* o_done = bars + 16;      // last P V done (commit)
+  uint64_t* drain = bars + 17;       // MMA drain before TMEM is freed
+  uint64_t* xbar = bars + 18;        // [quadrant][parity] row exchange between a row's two halves (2 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  static_assert(26 * 8 + 8 <= BAR_BYTES, "barrier region");
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y, batch = blockIdx.z;
-  const int q0 = blockIdx.x * 2 * BQ;
+  const int q0 = blockIdx.x * BQ;
   const int tiles = (sh.seq_kv + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < K_SLOTS; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
-      mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&k_empty[s]), 1);
-      mbar_init(smem_u32(&v_empty[s]), 1);
-      mbar_init(smem_u32(&s_full[s]), 1);
-      mbar_init(smem_u32(&p_full[s]), SOFTMAX_WARPS / 2);
-      mbar_init(smem_u32(&o_done[s]), 1);
     }
+    for (int s = 0; s < V_SLOTS; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&s_full[s]), 1);
+      mbar_init(smem_u32(&p_full[s]), SOFTMAX_WARPS);
+    }
+    mbar_init(smem_u32(pv_done), 1);
+    mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(drain), 1);
-    for (int b = 0; b < 16; ++b) mbar_init(smem_u32(&red_bar[b]), 2);
+    for (int b = 0; b < 8; ++b) mbar_init(smem_u32(&xbar[b]), 2);
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&map_q);
@@ -339,46 +350,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
+      // K runs two tiles ahead of V (Q K_{j+2}^T is issued right after P_j V_j):
+      // K_0 K_1 K_2 V_0 K_3 V_1 ...
       const int32_t x0 = head * D;
       const uint32_t qb = smem_u32(q_full);
-      mbar_expect_tx(qb, 2 * TILE);
-      for (int t = 0; t < 2; ++t) {
-        tma_load_3d(smem_u32(smem + SMEM_Q + t * TILE), &map_q, qb, x0, q0 + t * BQ, batch);
-        tma_load_3d(smem_u32(smem + SMEM_Q + t * TILE + ATOM), &map_q, qb, x0 + 64, q0 + t * BQ, batch);
-      }
-      bool issued[4] = {false, false, false, false};  // k0 k1 v0 v1
-      uint32_t issued_phase[4] = {0u, 0u, 0u, 0u};
+      mbar_expect_tx(qb, TILE);
+      tma_load_3d(smem_u32(smem + SMEM_Q), &map_q, qb, x0, q0, batch);
+      tma_load_3d(smem_u32(smem + SMEM_Q + ATOM), &map_q, qb, x0 + 64, q0, batch);
+      bool issued[K_SLOTS + V_SLOTS] = {};
+      uint32_t issued_phase[K_SLOTS + V_SLOTS] = {};
       bool ok = true;
-      for (int i = 0; i <= tiles && ok; ++i) {
-        if (i < tiles) {
-          const int st = i & 1;
-          const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-          if (!wait_bounded(smem_u32(&k_empty[st]), ph ^ 1u, abort_flag)) {
+      for (int i = 0; i < tiles + 2 && ok; ++i) {
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          const int j = kv == 0 ? i : i - 2;  // K_i, then V_{i-2}
+          if (j < 0 || j >= tiles) continue;
+          const int nslot = kv == 0 ? K_SLOTS : V_SLOTS;
+          const int st = j % nslot;
+          const uint32_t ph = (uint32_t)(j / nslot) & 1u;
+          if (!wait_bounded(smem_u32(kv == 0 ? &k_empty[st] : &v_empty[st]), ph ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t fb = smem_u32(&k_full[st]);
-          uint8_t* dst = smem + SMEM_K + st * TILE;
+          const uint32_t fb = smem_u32(kv == 0 ? &k_full[st] : &v_full[st]);
+          uint8_t* dst = smem + (kv == 0 ? SMEM_K : SMEM_V) + st * TILE;
+          const CUtensorMap* map = kv == 0 ? &map_k : &map_v;
           mbar_expect_tx(fb, TILE);
-          tma_load_3d(smem_u32(dst), &map_k, fb, x0, i * BKV, batch);
-          tma_load_3d(smem_u32(dst + ATOM), &map_k, fb, x0 + 64, i * BKV, batch);
-          issued[st] = true;
-          issued_phase[st] = ph;
-        }
-        if (i >= 1) {
-          const int j = i - 1, st = j & 1;
-          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-          if (!wait_bounded(smem_u32(&v_empty[st]), ph ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&v_full[st]);
-          uint8_t* dst = smem + SMEM_V + st * TILE;
-          mbar_expect_tx(fb, TILE);
-          tma_load_3d(smem_u32(dst), &map_v, fb, x0, j * BKV, batch);
-          tma_load_3d(smem_u32(dst + ATOM), &map_v, fb, x0 + 64, j * BKV, batch);
-          issued[2 + st] = true;
-          issued_phase[2 + st] = ph;
+          tma_load_3d(smem_u32(dst), map, fb, x0, j * BKV, batch);
+          tma_load_3d(smem_u32(dst + ATOM), map, fb, x0 + 64, j * BKV, batch);
+          issued[kv * K_SLOTS + st] = true;
+          issued_phase[kv * K_SLOTS + st] = ph;
         }
       }
       // Let every copy issued by this thread land before the CTA can exit.
@@ -386,9 +386,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       while (!mbar_try_wait(qb, 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
       }
       if (!ok)
-        for (int s = 0; s < 4; ++s)
+        for (int s = 0; s < K_SLOTS + V_SLOTS; ++s)
           if (issued[s]) {
-            const uint32_t fb = smem_u32(s < 2 ? &k_full[s] : &v_full[s - 2]);
+            const uint32_t fb = smem_u32(s < K_SLOTS ? &k_full[s] : &v_full[s - K_SLOTS]);
             const unsigned long long t1 = globaltimer();
             while (!mbar_try_wait(fb, issued_phase[s]) && globaltimer() - t1 < kWaitLimitNs / 4) {
             }
@@ -400,54 +400,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = wait_bounded(smem_u32(q_full), 0u, abort_flag);
       tc_fence_after();
       const uint32_t qa = smem_u32(smem + SMEM_Q);
-      // S_T(j) = Q_T K_j^T into TMEM columns [128 T, 128 T + 128).
-      auto issue_qk = [&](int t, int j) {
-        const uint32_t ka = smem_u32(smem + SMEM_K + (j & 1) * TILE);
+      // S(j) = Q K_j^T into score buffer j & 1.
+      auto issue_qk = [&](int j) {
+        const uint32_t ka = smem_u32(smem + SMEM_K + (j % K_SLOTS) * TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * ATOM + (kk & 3) * 32);
-          mma_f16(tmem + (uint32_t)(t * BQ), desc_kmajor(qa + t * TILE + off), desc_kmajor(ka + off), kIdescQK,
+          mma_f16(tmem + (uint32_t)((j & 1) * BKV), desc_kmajor(qa + off), desc_kmajor(ka + off), kIdescQK,
                   kk != 0 ? 1u : 0u);
         }
-        mma_commit(smem_u32(&s_full[t]));
+        mma_commit(smem_u32(&s_full[j & 1]));
+        mma_commit(smem_u32(&k_empty[j % K_SLOTS]));
       };
-      // O_T += P_T(j) V_j, P_T from TMEM columns [128 T, 128 T + 64).
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t va = smem_u32(smem + SMEM_V + (j & 1) * TILE);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_f16_ts(tmem + COL_O + (uint32_t)(t * D), tmem + (uint32_t)(t * BQ + kk * 8),
-                     desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV, (j | kk) != 0 ? 1u : 0u);
-      };
-      if (ok && wait_bounded(smem_u32(&k_full[0]), 0u, abort_flag)) {
+      for (int j = 0; j < 2 && j < tiles && ok; ++j) {
+        if (!wait_bounded(smem_u32(&k_full[j]), 0u, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        issue_qk(0, 0);
-        issue_qk(1, 0);
-        mma_commit(smem_u32(&k_empty[0]));
-      } else {
-        ok = false;
+        issue_qk(j);
       }
       for (int j = 0; j < tiles && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        const bool next = j + 1 < tiles;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!wait_bounded(smem_u32(&p_full[t]), (uint32_t)j & 1u, abort_flag) ||
-              (t == 0 && !wait_bounded(smem_u32(&v_full[st]), ph, abort_flag)) ||
-              (t == 0 && next &&
-               !wait_bounded(smem_u32(&k_full[st ^ 1]), (uint32_t)((j + 1) >> 1) & 1u, abort_flag))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (t == 1) mma_commit(smem_u32(&v_empty[st]));
-          if (!next) mma_commit(smem_u32(&o_done[t]));
-          if (next) {
-            issue_qk(t, j + 1);
-            if (t == 1) mma_commit(smem_u32(&k_empty[st ^ 1]));
-          }
+        const int nx = j + 2;
+        if (!wait_bounded(smem_u32(&p_full[j & 1]), (uint32_t)(j >> 1) & 1u, abort_flag) ||
+            !wait_bounded(smem_u32(&v_full[j % V_SLOTS]), (uint32_t)(j / V_SLOTS) & 1u, abort_flag) ||
+            (nx < tiles &&
+             !wait_bounded(smem_u32(&k_full[nx % K_SLOTS]), (uint32_t)(nx / K_SLOTS) & 1u, abort_flag))) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        // O += P(j) V_j, P(j) read from tensor memory (its score buffer).
+        const uint32_t va = smem_u32(smem + SMEM_V + (j % V_SLOTS) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          mma_f16_ts(tmem + COL_O, tmem + (uint32_t)((j & 1) * BKV + kk * 8),
+                     desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV, (j | kk) != 0 ? 1u : 0u);
+        mma_commit(smem_u32(pv_done));
+        mma_commit(smem_u32(&v_empty[j % V_SLOTS]));
+        if (j == tiles - 1) mma_commit(smem_u32(o_done));
+        if (nx < tiles) issue_qk(nx);  // into the buffer P(j) V_j just read (same order on the tensor core)
       }
       // Wait for every MMA this thread issued before TMEM can be released.
       mma_commit(smem_u32(drain));
@@ -457,22 +449,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // -------------------------------------------------------- softmax warps
-    const int idx = warp - 2;
-    const int t = idx >> 3;              // query tile: 0 = A (warps 2-9), 1 = B (warps 10-17)
-    const int half = (idx >> 2) & 1;     // keys / output columns [64 half, 64 half + 64)
-    const int quad = warp & 3;           // TMEM lanes [32 quad, 32 quad + 32)
+    const int quad = warp & 3;          // TMEM lanes [32 quad, 32 quad + 32)
+    const int half = (warp - 2) >> 2;   // keys / output columns [64 half, 64 half + 64)
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + (uint32_t)(t * BQ);
-    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(t * D + half * 64);
-    float* red = reinterpret_cast<float*>(smem + SMEM_RED) + t * 2 * 2 * BQ;  // [parity][half][row]
-    uint64_t* xbar = red_bar + t * 8 + quad * 2;                               // [parity]
+    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(half * 64);
+    float* red = reinterpret_cast<float*>(smem + SMEM_RED);  // [parity][half][row]
+    uint64_t* xq = xbar + quad * 2;                          // [parity]
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < tiles; ++j) {
       const int par = j & 1;
-      // S_T(j) ready; this also means P_T(j-1) V_{j-1} is done (same commit).
-      if (!warp_wait(smem_u32(&s_full[t]), (uint32_t)par, abort_flag, lane)) {
+      const uint32_t s_col = tmem + lane_off + (uint32_t)(par * BKV);
+      // S(j) ready; the same commit covers P(j-2) V_{j-2} (issued before).
+      if (!warp_wait(smem_u32(&s_full[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
         ok = false;
         break;
       }
@@ -503,21 +493,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mx2 = fmaxf(mx2, s[e + 2]);
         mx3 = fmaxf(mx3, s[e + 3]);
       }
-      // Row max over both halves: publish, then wait (bounded) for the partner
-      // warp's value of this tile parity. A slot is rewritten two tiles later,
-      // after the partner has read it (it must arrive again in between).
+      // Row max over both halves. Both halves have loaded their scores before
+      // either passes this exchange, so P (which overwrites score columns of
+      // the other half) is only written afterwards. A slot is rewritten two
+      // tiles later, after the partner has read it.
       red[(par * 2 + half) * BQ + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&xbar[par]));
-      if (!warp_wait(smem_u32(&xbar[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
+      if (lane == 0) mbar_arrive(smem_u32(&xq[par]));
+      if (!warp_wait(smem_u32(&xq[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
         ok = false;
         break;
       }
-      const float tile_max =
-          fmaxf(red[(par * 2) * BQ + row], red[(par * 2 + 1) * BQ + row]) * sh.scale_log2;
-      // Move the reference max only when it grows by more than 2^8: p <= 256,
-      // no overflow, and O is rescaled rarely (exact: O and l share it). Both
-      // halves of a row decide identically.
+      const float tile_max = fmaxf(red[(par * 2) * BQ + row], red[(par * 2 + 1) * BQ + row]) * sh.scale_log2;
+      // Move the reference max only when it grows by more than 2^8 (both
+      // halves decide identically): p <= 256, O rescaled rarely, exact.
       const bool move = tile_max > m_run + 8.0f;
       const float m_use = move ? tile_max : m_run;
       const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on the first tile
@@ -530,13 +519,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           softmax_half<LR_ATTN_EMU>(s, sc2, nm2, lsum, pk);
         else  // masked keys need an exact 0: MUFU only
           softmax_half<0>(s, sc2, nm2, lsum, pk);
-        tmem_st32(s_col + (uint32_t)(half * 32), pk);  // P over the consumed score columns
+        tmem_st32(s_col + (uint32_t)(half * 32), pk);  // P(j) keys [64 half, +64) as bf16 pairs
       }
       l_run = fmaf(l_run, alpha, lsum.x + lsum.y);
       m_run = m_use;
-      // O_T rescale of this half's 64 columns; P_T(j) V_j cannot start before
-      // the p_full arrive below.
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O must be stable: wait for P(j-1) V_{j-1} (at most one pending).
+        if (!warp_wait(smem_u32(pv_done), (uint32_t)(j - 1) & 1u, abort_flag, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         uint32_t oa[32], ob[32];
         tmem_ld32_nowait(o_col, oa);
         tmem_ld32_nowait(o_col + 32u, ob);
@@ -552,7 +545,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[par]));
     }
     // Each half holds the row sum over its keys against the same max; the
     // exchange uses the parity the last tile did not (read by both already).
@@ -561,14 +554,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int pe = tiles & 1;
       red[(pe * 2 + half) * BQ + row] = l_run;
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&xbar[pe]));
-      ok = warp_wait(smem_u32(&xbar[pe]), (uint32_t)(tiles >> 1) & 1u, abort_flag, lane);
+      if (lane == 0) mbar_arrive(smem_u32(&xq[pe]));
+      ok = warp_wait(smem_u32(&xq[pe]), (uint32_t)(tiles >> 1) & 1u, abort_flag, lane);
       if (ok) l_other = red[(pe * 2 + 1 - half) * BQ + row];
     }
-    if (ok && warp_wait(smem_u32(&o_done[t]), 0u, abort_flag, lane)) {
+    if (ok && warp_wait(smem_u32(o_done), 0u, abort_flag, lane)) {
       tc_fence_after();
       const float inv_l = 1.0f / (half == 0 ? l_run + l_other : l_other + l_run);
-      const int qrow = q0 + t * BQ + row;
+      const int qrow = q0 + row;
       uint32_t oa[32], ob[32];
       tmem_ld32_nowait(o_col, oa);
       tmem_ld32_nowait(o_col + 32u, ob);
@@ -616,13 +609,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [batch, seq, heads*128] bf16 with token stride `ts` elements: boxes of
-// 128 tokens x 64 columns, 128-byte swizzle, zero fill past the sequence.
-int make_map(CUtensorMap* map, const void* base, int64_t heads, int64_t seq, int64_t batch, int64_t ts) {
+// box_rows tokens x 64 columns, 128-byte swizzle, zero fill past the sequence.
+int make_map(CUtensorMap* map, const void* base, int64_t heads, int64_t seq, int64_t batch, int64_t ts,
+             uint32_t box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(LR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)(heads * D), (cuuint64_t)seq, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(ts * 2), (cuuint64_t)(seq * ts * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -668,11 +662,11 @@ extern "C" int lr_attention_bf16(const void* q, int64_t q_token_stride, const vo
   LR_REQUIRE(seq_q <= INT32_MAX && seq_kv <= INT32_MAX && heads <= 65535 && batch <= 65535,
              "attention: shape too large");
   CUtensorMap mq, mk, mv;
-  int st = attn::make_map(&mq, q, heads, seq_q, batch, q_token_stride);
+  int st = attn::make_map(&mq, q, heads, seq_q, batch, q_token_stride, attn::BQ);
   if (st) return st;
-  st = attn::make_map(&mk, k, heads, seq_kv, batch, k_token_stride);
+  st = attn::make_map(&mk, k, heads, seq_kv, batch, k_token_stride, attn::BKV);
   if (st) return st;
-  st = attn::make_map(&mv, v, heads, seq_kv, batch, v_token_stride);
+  st = attn::make_map(&mv, v, heads, seq_kv, batch, v_token_stride, attn::BKV);
   if (st) return st;
   static bool configured[64] = {};
   int dev = 0;
@@ -689,7 +683,7 @@ extern "C" int lr_attention_bf16(const void* q, int64_t q_token_stride, const vo
   sh.heads = (int)heads;
   sh.out_ts = out_token_stride;
   sh.scale_log2 = (float)((double)scale * 1.4426950408889634);
-  const dim3 grid((unsigned)((seq_q + 2 * attn::BQ - 1) / (2 * attn::BQ)), (unsigned)heads, (unsigned)batch);
+  const dim3 grid((unsigned)((seq_q + attn::BQ - 1) / attn::BQ), (unsigned)heads, (unsigned)batch);
   attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       mq, mk, mv, sh, static_cast<__nv_bfloat16*>(out));
   return launch_status("attention");
