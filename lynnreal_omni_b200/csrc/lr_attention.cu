@@ -668,14 +668,19 @@ extern "C" int lr_attention_bf16(const void* q, int64_t q_token_stride, const vo
   if (st) return st;
   st = attn::make_map(&mv, v, heads, seq_kv, batch, v_token_stride, attn::BKV);
   if (st) return st;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn::SMEM_BYTES) != cudaSuccess)
-      return launch_status("attention: configuring shared memory");
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+  {
+    // Opt in to the kernel's shared memory once per device (any host thread).
+    static std::mutex mu;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      if (cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)attn::SMEM_BYTES) != cudaSuccess)
+        return launch_status("attention: configuring shared memory");
+      if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
   }
   attn::Shape sh;
   sh.seq_q = (int)seq_q;

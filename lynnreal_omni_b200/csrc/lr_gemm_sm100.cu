@@ -1010,8 +1010,11 @@ int raster_group(int block_rows, int num_m, int K) {
 
 template <typename Kernel>
 int configure_smem(Kernel kernel, size_t bytes, bool (&done)[64]) {
+  // Once per device and kernel, from any host thread.
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < 64 && done[dev]) return LR_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
       cudaSuccess)

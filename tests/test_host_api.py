@@ -56,9 +56,35 @@ def test_empty_rows_are_a_no_op():
 
 
 def test_ops_refuse_cpu_tensors():
-    from lynnreal_omni_b200 import kernels as K
+    """No CPU path behind the product functions: host tensors are an error."""
+    from types import SimpleNamespace
+    from lynnreal_omni_b200 import kernels as K, flash
+    from lynnreal_omni_b200.attention import attention_bshd
     with pytest.raises(ValueError):
         K.quantize_rows(torch.zeros(2, 8, dtype=torch.bfloat16))
+    x = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        attention_bshd(x, x, x)
+    norm = SimpleNamespace(weight=torch.ones(128, dtype=torch.bfloat16), eps=1e-6)
+    with pytest.raises(ValueError):
+        K.qk_norm_rope(x, x, norm, norm, (torch.ones(4, 128), torch.zeros(4, 128)))
+    with pytest.raises(ValueError):
+        flash.index_select(torch.zeros(4, 8), 0, torch.tensor([1, 2]))
+    h = torch.zeros(1, 4, 8, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        flash.restore(h, h, h, torch.zeros(4, dtype=torch.int64))
+    with pytest.raises(ValueError):
+        flash.spatial_layout(torch.zeros(4, 3), torch.zeros(4, dtype=torch.int64))
+
+
+def test_empty_and_degenerate_calls_are_no_ops():
+    lib = _lib.load()
+    assert lib.lr_gather_rows(None, 0, 0, 0, 0, None, 0, None, 0, None) == _lib.LR_OK
+    assert lib.lr_flash_restore(None, None, None, None, 0, 0, 0, 0, 1.0, None, None) == _lib.LR_OK
+    assert lib.lr_flash_nearest_anchor(None, 0, None, 0, None, 0, None, None) == _lib.LR_OK
+    assert lib.lr_attention_bf16(None, 128, None, 128, None, 128, 0, 0, 0, 1, 128, 1.0, None, 128, None) == _lib.LR_OK
+    assert lib.lr_attention_bf16(None, 128, None, 128, None, 128, 1, 4, 4, 1, 64, 1.0, None, 128, None) == \
+        _lib.LR_ERR_UNSUPPORTED
 
 
 def test_int8_linear_contract():
