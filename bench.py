@@ -54,6 +54,9 @@ def parse_args():
                         "block at the released Flash shapes through the fused-block caller, attention included")
     p.add_argument("--layers", type=int, default=42)
     p.add_argument("--stack-tokens", type=int, default=64512)
+    p.add_argument("--compress", action="store_true",
+                   help="stack: Flash token compression in blocks 2-27 of a 21x48x64 video grid (the released "
+                        "schedule), shards of whole frames")
     return p.parse_args()
 
 
@@ -440,7 +443,20 @@ def run_stack(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     _lib.load()
     total = args.stack_tokens
-    start_row, stop_row = shard_bounds(total, world, rank)
+    comp = None
+    bounds = None
+    if args.compress:
+        from lynnreal_omni_b200.parallel import frame_bounds
+        grid_h, grid_w = 48, 64
+        if total % (grid_h * grid_w):
+            raise SystemExit("--compress needs --stack-tokens a multiple of 48 x 64")
+        frames = total // (grid_h * grid_w)
+        bounds = [frame_bounds(frames, grid_h * grid_w, world, r) for r in range(world)]
+        start_row, stop_row = bounds[rank]
+        comp = S.Compression((stop_row - start_row) // (grid_h * grid_w), grid_h, grid_w, dev,
+                             end=min(28, args.layers - 1), first_frame=start_row // (grid_h * grid_w))
+    else:
+        start_row, stop_row = shard_bounds(total, world, rank)
     m = stop_row - start_row
     model = S.FlashStackW8A8(args.layers, dev, seed=0)
     g = W.generator(100 + rank, dev)
@@ -452,8 +468,9 @@ def run_stack(args, rank, world, local):
         if world > 1:
             dist.barrier()
 
-    def step(ev=None):
-        return model.sharded_forward(x_local, total, world, rank, idx, ctx, ffn_events=ev)
+    def step(ev=None, xin=None):
+        return model.sharded_forward(x_local if xin is None else xin, total, world, rank, idx, ctx, ffn_events=ev,
+                                     compression=comp, bounds=bounds)
 
     for _ in range(args.warmup):
         step()
@@ -489,7 +506,7 @@ def run_stack(args, rank, world, local):
     e0.record()
     for _ in range(args.steps):
         x_d.copy_(x_h, non_blocking=True)
-        res = model.sharded_forward(x_d, total, world, rank, idx, ctx)
+        res = step(xin=x_d)
         out_h.copy_(res.view(total, W.HIDDEN) if world > 1 else res.view(-1, W.HIDDEN), non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -503,10 +520,18 @@ def run_stack(args, rank, world, local):
         peak = 2.0 * (peaks.get("bf16_tflops") or FALLBACK_BF16_BURST_TFLOPS)
         up_ops = 2.0 * m * W.FFN * W.HIDDEN
         achieved = up_ops / (ffn_ms / 1e3) / 1e12
+        if comp is not None:
+            kept = comp.kept_rows()
+            glob_kept = kept * world  # frames are alike: every full frame keeps the same rows
+            token_passes = S.DENOISER_STEPS * (total * (args.layers - (comp.end - comp.start)) +
+                                               glob_kept * (comp.end - comp.start))
+        else:
+            token_passes = total * passes
         line = {
-            "metric": METRIC,
-            "value": total * passes * args.steps / (elapsed_ms / 1e3),
-            "unit": "tokens/s (block-token passes: tokens x blocks x denoiser steps)",
+            "metric": METRIC if comp is None else "Flash stack latent tokens/s (token compression in blocks 2-27)",
+            "value": (total * passes if comp is None else total * S.DENOISER_STEPS) * args.steps / (elapsed_ms / 1e3),
+            "unit": ("tokens/s (block-token passes: tokens x blocks x denoiser steps)" if comp is None
+                     else "latent tokens/s (tokens x denoiser steps)"),
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; random-init int8 weights)",
@@ -518,14 +543,19 @@ def run_stack(args, rank, world, local):
                        "parallelism": f"dp{world} over token rows, weights replicated, all-gather at the end",
                        "l2": "no flush: 24.4 GB of weights streamed per denoiser step"},
             "latent_tokens_per_s": total * S.DENOISER_STEPS * args.steps / (elapsed_ms / 1e3),
+            "block_token_passes_per_s": token_passes * args.steps / (elapsed_ms / 1e3),
+            "compression": None if comp is None else {
+                "grid": [total // 3072, 48, 64], "kept_rows_per_rank": comp.kept_rows(),
+                "compressed_blocks": [comp.start, comp.end], "shards": "whole frames"},
             "roofline": {"kernel": f"ffn_up int8 GEMM + GELU (CTA-pair gemm_tc2_kernel<kGelu>), M={m} K={W.HIDDEN} N={W.FFN}",
                          "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s (int8)",
                          "frac": achieved / peak, "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
                          "launch_ms": ffn_ms, "traffic": None},
             "clocks": clocks,
-            "gpu_launches": model.launches_per_forward() * args.steps,
+            "gpu_launches": (model.launches_per_forward() + (2 * S.DENOISER_STEPS if comp is not None else 0)) * args.steps,
             "device_status": status,
-            "e2e": {"value": total * passes * args.steps / (te.item() / 1e3), "unit": "tokens/s",
+            "e2e": {"value": (total * passes if comp is None else total * S.DENOISER_STEPS) * args.steps
+                              / (te.item() / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_h.numel() * 2, "d2h_bytes_per_step": out_h.numel() * 2,
                     "ms_per_step": te.item() / args.steps},
         }

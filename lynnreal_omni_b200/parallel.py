@@ -28,26 +28,36 @@ def shard_rows(x: torch.Tensor, world: int, rank: int, dim: int = -2) -> torch.T
     return x.narrow(dim, start, stop - start)
 
 
-def gather_rows(local: torch.Tensor, total: int, group=None) -> torch.Tensor:
+def frame_bounds(frames: int, frame_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) rows of this rank when whole frames of ``frame_rows`` rows
+    are distributed (first ranks get the remainder). Token compression selects
+    and restores within a frame, so frame-aligned shards compress exactly as
+    the whole sequence does."""
+    f0, f1 = shard_bounds(frames, world, rank)
+    return f0 * frame_rows, f1 * frame_rows
+
+
+def gather_rows(local: torch.Tensor, total: int, group=None, bounds=None) -> torch.Tensor:
     """All-gather the row blocks of every rank into the full [total, ...] tensor.
 
-    ``local`` is this rank's block (rows on dim 0). One all_gather_into_tensor
-    of equally padded shards; the result is identical on every rank.
+    ``local`` is this rank's block (rows on dim 0); ``bounds[r]`` is rank r's
+    [start, stop) (default: ``shard_bounds``). One all_gather_into_tensor of
+    equally padded shards; the result is identical on every rank.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    start, stop = shard_bounds(total, world, rank)
+    bounds = bounds or [shard_bounds(total, world, r) for r in range(world)]
+    if len(bounds) != world or bounds[0][0] != 0 or bounds[-1][1] != total or any(
+            bounds[r][1] != bounds[r + 1][0] for r in range(world - 1)):
+        raise ValueError("row bounds must tile [0, total) in rank order")
+    start, stop = bounds[rank]
     if local.shape[0] != stop - start:
         raise ValueError(f"rank {rank} holds {local.shape[0]} rows, expected {stop - start}")
-    width = -(-total // world)
+    width = max(e - s for s, e in bounds)
     padded = local.new_zeros((width, *local.shape[1:]))
     padded[: local.shape[0]] = local
     out = local.new_empty((world * width, *local.shape[1:]))
     dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
-    if total % world == 0:
+    if all(e - s == width for s, e in bounds):
         return out
-    parts = []
-    for r in range(world):
-        s, e = shard_bounds(total, world, r)
-        parts.append(out[r * width: r * width + (e - s)])
-    return torch.cat(parts, dim=0)
+    return torch.cat([out[r * width: r * width + (e - s)] for r, (s, e) in enumerate(bounds)], dim=0)

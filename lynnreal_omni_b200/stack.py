@@ -14,6 +14,7 @@ import torch
 
 from . import block as B
 from . import workloads as W
+from . import flash
 from .parallel import gather_rows, shard_rows
 
 LAYERS = 42
@@ -32,25 +33,67 @@ class FlashStackW8A8:
         self.steps = steps
 
     def forward(self, x_local: torch.Tensor, indices: torch.Tensor, context: torch.Tensor,
-                ffn_events=None) -> torch.Tensor:
+                ffn_events=None, compression: "Compression | None" = None) -> torch.Tensor:
         """x_local bf16 [1, m, D] (this rank's token rows) -> bf16 [1, m, D] after
         every denoiser step's pass through every block. ``ffn_events`` bracket
-        the FFN-up GEMM of the first block of the first step."""
+        the FFN-up GEMM of the first block of the first step. With
+        ``compression``, blocks [start, end) of every step run on the kept rows
+        and the residual is restored before block ``end`` (model/flash.py:65-84)."""
         h = x_local
         for s, step_tables in enumerate(self.tables):
+            full = start_rows = None
             for i, (blk, table) in enumerate(zip(self.blocks, step_tables)):
-                h, _ = blk(h, table, indices, context, ffn_events=ffn_events if s == 0 and i == 0 else None)
+                idx = indices
+                if compression is not None:
+                    if i == compression.start:
+                        full = h
+                        h = start_rows = flash.index_select(h, 1, compression.keep)
+                    if i == compression.end:
+                        h = flash.restore(full, h, start_rows, compression.inverse, compression.gain)
+                    if compression.start <= i < compression.end:
+                        idx = compression.indices(indices)
+                h, _ = blk(h, table, idx, context, ffn_events=ffn_events if s == 0 and i == 0 else None)
         return h
 
     def launches_per_forward(self) -> int:
         return self.steps * len(self.blocks) * B.LAUNCHES_PER_FORWARD
 
     def sharded_forward(self, x_full_or_local, total_tokens: int, world: int, rank: int, indices, context,
-                        gather: bool = True, ffn_events=None):
-        """Run this rank's rows and all-gather the bf16 outputs ([total, D])."""
+                        gather: bool = True, ffn_events=None, compression: "Compression | None" = None,
+                        bounds=None):
+        """Run this rank's rows and all-gather the bf16 outputs ([total, D]);
+        ``bounds`` are every rank's row blocks when they are not the default
+        even split (frame-aligned shards for compression)."""
         local = x_full_or_local if x_full_or_local.shape[-2] != total_tokens else shard_rows(
             x_full_or_local, world, rank)
-        out = self.forward(local.contiguous(), indices, context, ffn_events=ffn_events)
+        out = self.forward(local.contiguous(), indices, context, ffn_events=ffn_events, compression=compression)
         if not gather or world == 1:
             return out
-        return gather_rows(out.view(-1, out.shape[-1]), total_tokens)
+        return gather_rows(out.view(-1, out.shape[-1]), total_tokens, bounds=bounds)
+
+
+class Compression:
+    """Flash token compression of a video grid (frames x rows x columns,
+    row-major rows): the kept rows and each row's restore source from
+    ``flash.spatial_layout``; blocks [start, end) run compressed (the released
+    schedule: 2 and 28 of 42)."""
+
+    def __init__(self, frames: int, height: int, width: int, device, start: int = 2, end: int = 28,
+                 gain: float = 1.0, first_frame: int = 0):
+        t, h, w = torch.meshgrid(torch.arange(first_frame, first_frame + frames), torch.arange(height),
+                                 torch.arange(width), indexing="ij")
+        positions = torch.stack([t, h, w], -1).reshape(-1, 3).to(device)
+        tags = torch.zeros(positions.shape[0], dtype=torch.int64, device=device)
+        self.keep, self.inverse = flash.spatial_layout(positions, tags)
+        self.start, self.end, self.gain = start, end, gain
+        self._indices = {}
+
+    def indices(self, indices: torch.Tensor) -> torch.Tensor:
+        """adaLN indices of the kept rows (gathered once per indices tensor)."""
+        key = (indices.data_ptr(), indices.numel())
+        if key not in self._indices:
+            self._indices[key] = flash.index_select(indices, 0, self.keep)
+        return self._indices[key]
+
+    def kept_rows(self) -> int:
+        return self.keep.numel()

@@ -164,3 +164,33 @@ def test_configure_flash_contract():
         model(x, x[:, 0], pos, torch.zeros(3, dtype=torch.int64, device=DEV),
               (torch.zeros(3, 4, device=DEV), torch.zeros(3, 4, device=DEV)), torch.zeros(3, dtype=torch.int64,
                                                                                         device=DEV))
+
+
+def test_compressed_stack_equals_the_hook_schedule():
+    """stack.FlashStackW8A8 with token compression (blocks [1, 3) of 4, two
+    denoiser steps) equals the same blocks run with the reference hooks'
+    schedule written in torch ops: gather the kept rows before block 1,
+    restore full + ((out - in) * gain)[inverse] before block 3."""
+    from lynnreal_omni_b200 import stack as S
+    frames, height, width, hidden = 2, 6, 10, 256
+    model = S.FlashStackW8A8(4, DEV, seed=5, hidden=hidden, ffn=512, text_dim=128, steps=2)
+    comp = S.Compression(frames, height, width, DEV, start=1, end=3, gain=0.75)
+    m = frames * height * width
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(1, m, hidden, device=DEV, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(16, 128, device=DEV, generator=g).to(torch.bfloat16)
+    idx = torch.zeros(m, dtype=torch.int64, device=DEV)
+    got = model.forward(x, idx, ctx, compression=comp)
+    h = x
+    for tables in model.tables:
+        for i, (blk, table) in enumerate(zip(model.blocks, tables)):
+            if i == 1:
+                full, h = h, h.index_select(1, comp.keep)
+                start = h
+            if i == 3:
+                h = full + ((h - start) * 0.75).index_select(1, comp.inverse)
+            ids = idx.index_select(0, comp.keep) if 1 <= i < 3 else idx
+            h, _ = blk(h, table, ids, ctx)
+    assert torch.equal(got, h)
+    assert comp.kept_rows() == frames * 4 * 6  # rows {0,2,4,5} x columns {0,2,4,6,8,9}
+    assert _lib.device_status(clear=True) == 0

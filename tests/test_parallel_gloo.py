@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from lynnreal_omni_b200.parallel import gather_rows, shard_bounds, shard_rows
+from lynnreal_omni_b200.parallel import frame_bounds, gather_rows, shard_bounds, shard_rows
 
 
 def _free_port() -> int:
@@ -30,27 +30,40 @@ def test_shard_bounds_cover_rows_exactly():
         shard_bounds(10, 2, 2)
 
 
-def _worker(rank, world, port, total, queue):
+def test_frame_bounds_are_whole_frames():
+    for frames, world in ((21, 8), (21, 2), (5, 4), (3, 3)):
+        spans = [frame_bounds(frames, 3072, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == frames * 3072
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert all(s % 3072 == 0 and e % 3072 == 0 for s, e in spans)
+
+
+def _worker(rank, world, port, total, queue, frames=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         full = torch.arange(total * 6, dtype=torch.float32).view(1, total, 6)
-        local = shard_rows(full, world, rank)
+        bounds = None
+        if frames:  # uneven whole-frame shards (token compression)
+            bounds = [frame_bounds(frames, total // frames, world, r) for r in range(world)]
+            local = full[:, bounds[rank][0]:bounds[rank][1]]
+        else:
+            local = shard_rows(full, world, rank)
         # stand-in for the per-rank W8A8 path: any row-local function
         out_local = (local * 2 + 1).view(-1, 6)
-        gathered = gather_rows(out_local, total)
+        gathered = gather_rows(out_local, total, bounds=bounds)
         queue.put((rank, torch.equal(gathered, (full * 2 + 1).view(total, 6))))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("total", [8, 13])
-def test_gather_rows_world2_gloo(total):
+@pytest.mark.parametrize("total,frames", [(8, 0), (13, 0), (15, 5)])
+def test_gather_rows_world2_gloo(total, frames):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, total, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, total, queue, frames)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(queue.get(timeout=120) for _ in procs)
