@@ -14,9 +14,10 @@
 #include "lr_common.cuh"
 #include "lr_host.h"
 
-// Minimum resident CTAs per SM requested for the persistent RMSNorm kernel
-// (a register cap: 4 -> 64 registers, 32 warps per SM; measured 5 % faster
-// than the compiler's 80 registers, 3 CTAs per SM). Tuning knob.
+// Minimum resident CTAs per SM requested for the persistent RMSNorm kernel on
+// rows of up to 4 chunks per thread (a register cap: 4 -> 64 registers, 32
+// warps per SM; measured 5 % faster than the compiler's 80 registers, 3 CTAs
+// per SM). Wider rows keep the compiler's allocation. Tuning knob.
 #ifndef LR_RMS_MINB
 #define LR_RMS_MINB 4
 #endif
@@ -197,7 +198,7 @@ __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4
 }
 
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
-__global__ void __launch_bounds__(kThreads, LR_RMS_MINB) rms_mod_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreads, (C <= 4 ? LR_RMS_MINB : 0)) rms_mod_kernel(const RmsArgs a) {
   __shared__ float red[kWarps];
   constexpr bool kPre = Prefetch<C>::kOn;
   constexpr int kN = Prefetch<C>::kN;
