@@ -21,6 +21,19 @@
 #ifndef LR_RMS_MINB
 #define LR_RMS_MINB 4
 #endif
+// The same caps for the two-row residual RMSNorm kernel (K8: 0, a cap measured
+// slower), for the quantiser on rows of more than 4 chunks per thread (K1 on
+// FFN widths: 4 -> 64 registers; 185 -> 140 us at 12240 x 24576, ~ the HBM copy
+// rate) and for the SwiGLU kernels (4: 292 -> 270 us at 12240 x 2 x 14336).
+#ifndef LR_RMS2_MINB
+#define LR_RMS2_MINB 0
+#endif
+#ifndef LR_QUANT_WIDE_MINB
+#define LR_QUANT_WIDE_MINB 4
+#endif
+#ifndef LR_SWIGLU_MINB
+#define LR_SWIGLU_MINB 4
+#endif
 
 namespace lr {
 
@@ -68,7 +81,7 @@ struct Prefetch {
 
 // --------------------------------------------------------------------- K1
 template <int C, bool VEC>
-__global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const bf16* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : 0)) quantize_rows_kernel(const bf16* __restrict__ x,
                                                                   int64_t row_stride, int width,
                                                                   int8_t* __restrict__ q,
                                                                   float* __restrict__ scales,
@@ -280,7 +293,7 @@ __device__ __forceinline__ float2 block_max2(float2 v, float2* scratch) {
 }
 
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
-__global__ void __launch_bounds__(kThreads) rms_mod2_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreads, LR_RMS2_MINB) rms_mod2_kernel(const RmsArgs a) {
   __shared__ float2 red[kWarps];
   const int hidden = a.hidden;
   const int64_t row0 = 2 * (int64_t)blockIdx.x;
@@ -447,13 +460,22 @@ __global__ void __launch_bounds__(kThreads) gated_residual_kernel(
 }
 
 // ------------------------------------------------------------------ K6/K7
+// 1: the sigmoid of SwiGLU uses the fast hardware exponential and division
+// (__expf, __fdividef), as the reference's compiled Triton kernel does
+// (tl.sigmoid lowers to ex2.approx and div.full); 0: expf and IEEE division.
+// Both reproduce the reference's golden SwiGLU outputs exactly; the fast form
+// runs the K7 kernel in 162 instead of 270 us at 12240 x 2 x 14336. Tuning knob.
+#ifndef LR_SWIGLU_FAST
+#define LR_SWIGLU_FAST 1
+#endif
 __device__ __forceinline__ float silu(float g) {
   // g * sigmoid(g), sigmoid(g) = 1 / (1 + exp(-g))   (model/kernels.py:165,177)
+  if (LR_SWIGLU_FAST) return __fmul_rn(g, __fdividef(1.0f, __fadd_rn(1.0f, __expf(-g))));
   return __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
 }
 
 template <int C, bool VEC, bool QUANT>
-__global__ void __launch_bounds__(kThreads) swiglu_kernel(const bf16* __restrict__ projected,
+__global__ void __launch_bounds__(kThreads, LR_SWIGLU_MINB) swiglu_kernel(const bf16* __restrict__ projected,
                                                           int inner, bf16* __restrict__ out,
                                                           int8_t* __restrict__ q,
                                                           float* __restrict__ scales,
