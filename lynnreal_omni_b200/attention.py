@@ -21,10 +21,12 @@ __all__ = ["attention_bshd"]
 
 
 def _token_view(t: torch.Tensor) -> torch.Tensor:
-    """[B, S, H, D] with unit element stride, heads contiguous and batch
-    stride = S * token stride, else a contiguous copy."""
+    """[B, S, H, D] with unit element stride, heads contiguous, batch stride =
+    S * token stride and 16-byte aligned rows (what the kernel's TMA maps
+    address), else a contiguous copy."""
     b, s, h, d = t.shape
-    if t.stride(3) == 1 and t.stride(2) == d and (b == 1 or t.stride(0) == s * t.stride(1)):
+    if (t.stride(3) == 1 and t.stride(2) == d and (b == 1 or t.stride(0) == s * t.stride(1))
+            and t.stride(1) % 8 == 0 and t.data_ptr() % 16 == 0):
         return t
     return t.contiguous()
 

@@ -90,7 +90,7 @@ class Compression:
 
     def indices(self, indices: torch.Tensor) -> torch.Tensor:
         """adaLN indices of the kept rows (gathered once per indices tensor)."""
-        key = (indices.data_ptr(), indices.numel())
+        key = (indices.data_ptr(), indices.numel(), indices._version, tuple(indices.stride()))
         if key not in self._indices:
             self._indices[key] = flash.index_select(indices, 0, self.keep)
         return self._indices[key]

@@ -67,6 +67,18 @@ def test_attention_on_fused_qkv_views():
     check_close(got, reference(q, k, v, scale), q, k, v, scale)
 
 
+def test_attention_on_misaligned_views():
+    """Views whose rows are not 16-byte aligned are copied, not refused."""
+    b, s, h = 1, 130, 2
+    g = torch.Generator(device=DEV).manual_seed(11)
+    base = torch.randn(b, s, h * 128 + 4, device=DEV, generator=g).to(torch.bfloat16)
+    q = base[..., 4:].unflatten(-1, (h, 128))  # token stride 260: rows 8-byte aligned only
+    k = torch.randn(b, s, h, 128, device=DEV, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, s, h, 128, device=DEV, generator=g).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(128)
+    check_close(attention_bshd(q, k, v), reference(q, k, v, scale), q, k, v, scale)
+
+
 def test_attention_rejects_unsupported():
     x = torch.zeros(1, 8, 2, 64, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
