@@ -88,6 +88,7 @@ def restore(full: torch.Tensor, compressed: torch.Tensor, compressed_input: torc
 def _retained(column: torch.Tensor, stride: int) -> torch.Tensor:
     """For video rows' coordinates on one axis: whether each survives stride
     selection over the sorted alphabet (every stride-th value, and the last)."""
+    column = column.contiguous()
     alphabet = torch.unique(column, sorted=True)
     rank = torch.searchsorted(alphabet, column)
     return (rank % stride == 0) | (rank == alphabet.numel() - 1)
@@ -127,72 +128,93 @@ def spatial_layout(positions: torch.Tensor, tags: torch.Tensor, stride: int = 2)
     return keep, inverse
 
 
+def _compression_span(config, depth: int) -> tuple[int, int, float]:
+    """Validate the checkpoint's token-compression settings (the only layout
+    the released hooks support) and return (first compressed block, first
+    restored block, residual gain)."""
+    c = config["token_compression"]
+    if depth != config["num_layers"]:
+        raise ValueError("Flash depth and exported weights disagree")
+    fixed = {"reduction": "select", "spatial_stride": 2}
+    if (any(c[name] != value for name, value in fixed.items())
+            or not (c["preserve_text_tokens"] and c["preserve_audio_tokens"])
+            or c.get("full_refresh_blocks") or c.get("text_stride", 1) != 1 or c.get("audio_stride", 1) != 1):
+        raise ValueError("unsupported Flash token layout")
+    first, restored = c["full_prefix_blocks"], depth - c["full_suffix_blocks"]
+    if not 0 < first < restored < depth:
+        raise ValueError("Flash requires nonempty full-resolution prefix and suffix")
+    return first, restored, float(c.get("residual_gain", 1.0))
+
+
+class _FlashHooks:
+    """Hook state of one configured transformer. ``on_forward`` (pre-hook of
+    the transformer) resolves the packed layout of this forward (cached while
+    positions and tags stay the same); ``on_compressed_block`` (pre-hook of
+    each compressed block) swaps in the kept rows — the hidden stream once,
+    the adaLN indices, rotary rows and mask once per forward; ``on_restore``
+    (pre-hook of the first suffix block) adds the compressed blocks' change
+    back onto the full sequence; ``on_done`` (forward hook, always called)
+    resets the per-forward state."""
+
+    def __init__(self, signature, gain: float):
+        self.signature = signature
+        self.gain = gain
+        self.layout = None        # (positions, tags, keep, inverse) of the last layout seen
+        self.active = False
+        self.full = None          # hidden stream entering the first compressed block
+        self.entry = None         # its compressed rows (the first compressed block's input)
+        self.selected = {}        # per-forward gathers of the unchanged block arguments
+
+    def on_forward(self, module, args, kwargs):
+        if module.training or torch.is_grad_enabled():
+            raise ValueError("Flash hooks require frozen inference")
+        if self.active:
+            raise RuntimeError("Flash transformer does not support concurrent forwards")
+        bound = self.signature.bind(*args, **kwargs).arguments
+        positions, tags = bound["position_ids"], bound["token_tags"]
+        known = self.layout
+        if not (known is not None and known[0].shape == positions.shape and known[1].shape == tags.shape
+                and torch.equal(positions, known[0]) and torch.equal(tags, known[1])):
+            self.layout = (positions.clone(), tags.clone(), *spatial_layout(positions, tags))
+        self.active = True
+
+    def _select(self, value, dim):
+        # the same tensor (identity, storage and version) gathers to the same rows
+        key = (id(value), value.data_ptr(), value._version, dim)
+        if key not in self.selected:
+            self.selected[key] = (value, index_select(value, dim, self.layout[2]))
+        return self.selected[key][1]
+
+    def on_compressed_block(self, module, args):
+        hidden, temb, indices, rotary, mask = args
+        if self.full is None:
+            self.full = hidden
+            hidden = self.entry = index_select(hidden, 1, self.layout[2])
+        return (hidden, temb, self._select(indices, 0), tuple(self._select(v, -2) for v in rotary),
+                None if mask is None else self._select(mask, -1))
+
+    def on_restore(self, module, args):
+        hidden = restore(self.full, args[0], self.entry, self.layout[3], self.gain)
+        self.full = self.entry = None
+        return (hidden, *args[1:])
+
+    def on_done(self, *_):
+        self.active = False
+        self.full = self.entry = None
+        self.selected = {}
+
+
 def configure_flash(transformer, config):
     """Install the Flash inference hooks (model/flash.py:36-94); weights and
     the transformer's own code stay as they are."""
     blocks = transformer.transformer_blocks
-    compression = config["token_compression"]
-    if len(blocks) != config["num_layers"]:
-        raise ValueError("Flash depth and exported weights disagree")
-    supported = (compression["reduction"] == "select" and compression["spatial_stride"] == 2
-                 and compression["preserve_text_tokens"] and compression["preserve_audio_tokens"]
-                 and not compression.get("full_refresh_blocks")
-                 and compression.get("text_stride", 1) == 1 and compression.get("audio_stride", 1) == 1)
-    if not supported:
-        raise ValueError("unsupported Flash token layout")
-    start = compression["full_prefix_blocks"]
-    end = len(blocks) - compression["full_suffix_blocks"]
-    if not 0 < start < end < len(blocks):
-        raise ValueError("Flash requires nonempty full-resolution prefix and suffix")
+    first, restored, gain = _compression_span(config, len(blocks))
     if hasattr(transformer, "_lynnreal_flash_hooks"):
         raise ValueError("Flash is already configured")
     transformer.h3_token_compression = None
-    gain = float(compression.get("residual_gain", 1.0))
-    signature = inspect.signature(transformer.forward)
-    state = {}
-    layout = {}
-
-    def begin(module, args, kwargs):
-        if module.training or torch.is_grad_enabled():
-            raise ValueError("Flash hooks require frozen inference")
-        if state:
-            raise RuntimeError("Flash transformer does not support concurrent forwards")
-        bound = signature.bind(*args, **kwargs).arguments
-        positions, tags = bound["position_ids"], bound["token_tags"]
-        same = (layout and layout["positions"].shape == positions.shape and layout["tags"].shape == tags.shape
-                and torch.equal(positions, layout["positions"]) and torch.equal(tags, layout["tags"]))
-        if not same:
-            keep, inverse = spatial_layout(positions, tags)
-            layout.update(positions=positions.clone(), tags=tags.clone(), keep=keep, inverse=inverse)
-        state["keep"], state["inverse"] = layout["keep"], layout["inverse"]
-        state["gathered"] = {}
-
-    def gathered(value, dim):
-        # the same tensor (identity, storage and version) gathers to the same rows
-        key = (id(value), value.data_ptr(), value._version, dim)
-        hit = state["gathered"].get(key)
-        if hit is None:
-            hit = state["gathered"][key] = (value, index_select(value, dim, state["keep"]))
-        return hit[1]
-
-    def compress(module, args):
-        hidden, temb, indices, rotary, mask = args
-        if "full" not in state:
-            state["full"] = hidden
-            hidden = index_select(hidden, 1, state["keep"])
-            state["input"] = hidden
-        return (hidden, temb, gathered(indices, 0), tuple(gathered(v, -2) for v in rotary),
-                None if mask is None else gathered(mask, -1))
-
-    def restore_hook(module, args):
-        hidden = restore(state.pop("full"), args[0], state.pop("input"), state["inverse"], gain)
-        return (hidden, *args[1:])
-
-    def finish(*_):
-        state.clear()
-
-    handles = [transformer.register_forward_pre_hook(begin, with_kwargs=True)]
-    handles += [block.register_forward_pre_hook(compress) for block in blocks[start:end]]
-    handles += [blocks[end].register_forward_pre_hook(restore_hook),
-                transformer.register_forward_hook(finish, always_call=True)]
+    hooks = _FlashHooks(inspect.signature(transformer.forward), gain)
+    handles = [transformer.register_forward_pre_hook(hooks.on_forward, with_kwargs=True)]
+    handles += [block.register_forward_pre_hook(hooks.on_compressed_block) for block in blocks[first:restored]]
+    handles.append(blocks[restored].register_forward_pre_hook(hooks.on_restore))
+    handles.append(transformer.register_forward_hook(hooks.on_done, always_call=True))
     transformer._lynnreal_flash_hooks = handles

@@ -85,9 +85,37 @@ def fuse_qkv(model, gemm: str = "triton") -> None:
         attn.fused_projections = True
 
 
-def _read_shard(path: Path, device):
+_METADATA = ("config.json", "quantization_config.json", "diffusion_pytorch_model.safetensors.index.json")
+
+
+def _verified_metadata(folder: Path, checksums: dict) -> list:
+    """The three metadata documents, each checked against its SHA-256 first."""
+    docs = []
+    for name in _METADATA:
+        if sha256(folder / name) != checksums[name]["sha256"]:
+            raise ValueError("Flash metadata checksum mismatch: " + name)
+        docs.append(json.loads((folder / name).read_text()))
+    return docs
+
+
+def _verified_tensors(folder: Path, weight_map: dict, checksums: dict, device) -> dict:
+    """All tensors of the checkpoint; every shard's size and SHA-256 are checked
+    before it is read, and its tensor names against the index."""
     from safetensors.torch import load_file
-    return load_file(str(path), device=str(device))
+    by_shard = {}
+    for tensor_name, shard in weight_map.items():
+        by_shard.setdefault(shard, set()).add(tensor_name)
+    tensors = {}
+    for shard in sorted(by_shard):
+        path = folder / shard
+        expect = checksums[shard]
+        if path.stat().st_size != expect["bytes"] or sha256(path) != expect["sha256"]:
+            raise ValueError("Flash shard checksum mismatch: " + shard)
+        loaded = load_file(str(path), device=str(device))
+        if set(loaded) != by_shard[shard]:
+            raise ValueError("Flash shard index mismatch")
+        tensors.update(loaded)
+    return tensors
 
 
 def load_transformer(folder, device="cuda", gemm="triton", model_factory=None):
@@ -95,27 +123,14 @@ def load_transformer(folder, device="cuda", gemm="triton", model_factory=None):
     (model/flash_int8.py:9-56); same checks and error messages."""
     folder = Path(folder).resolve(strict=True)
     checksums = json.loads((folder / "checksums.json").read_text())
-    for name in ("config.json", "quantization_config.json", "diffusion_pytorch_model.safetensors.index.json"):
-        if sha256(folder / name) != checksums[name]["sha256"]:
-            raise ValueError("Flash metadata checksum mismatch: " + name)
-    config = json.loads((folder / "config.json").read_text())
-    quant = json.loads((folder / "quantization_config.json").read_text())
-    index = json.loads((folder / "diffusion_pytorch_model.safetensors.index.json").read_text())["weight_map"]
+    config, quant, index = _verified_metadata(folder, checksums)
     model = (model_factory or _default_factory)(config)
-    remaining = set(model.state_dict())
-    pending = {}
-    for filename in sorted(set(index.values())):
-        path = folder / filename
-        if path.stat().st_size != checksums[filename]["bytes"] or sha256(path) != checksums[filename]["sha256"]:
-            raise ValueError("Flash shard checksum mismatch: " + filename)
-        tensors = _read_shard(path, device)
-        if set(tensors) != {k for k, v in index.items() if v == filename}:
-            raise ValueError("Flash shard index mismatch")
-        pending.update(tensors)
-    remaining.difference_update(install_packed(model, pending, quant["quantized_modules"], gemm))
-    if set(pending) != remaining:
-        raise ValueError("Incomplete Flash model: " + str(set(pending) ^ remaining))
-    result = model.load_state_dict(pending, strict=False, assign=True)
+    expected = set(model.state_dict())
+    tensors = _verified_tensors(folder, index["weight_map"], checksums, device)
+    expected -= install_packed(model, tensors, quant["quantized_modules"], gemm)
+    if set(tensors) != expected:
+        raise ValueError("Incomplete Flash model: " + str(set(tensors) ^ expected))
+    result = model.load_state_dict(tensors, strict=False, assign=True)
     if result.unexpected_keys:
         raise ValueError(result.unexpected_keys)
     fuse_qkv(model, gemm)

@@ -232,3 +232,112 @@ def test_flash_block_module_through_enable_fusion():
     assert torch.equal(got, expect)
     assert torch.isfinite(got.float()).all()
     assert _lib.device_status(clear=True) == 0
+
+
+# ------------------------------------------------------- bf16 block routes
+def _bf16_linear(n_in, n_out, gen):
+    lin = nn.Linear(n_in, n_out).to(torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_((torch.randn(n_out, n_in, generator=gen) / n_in ** 0.5).to(torch.bfloat16))
+        lin.bias.copy_((0.02 * torch.randn(n_out, generator=gen)).to(torch.bfloat16))
+    return lin
+
+
+def _native_norm(d, gen):
+    norm = nn.RMSNorm(d, eps=1e-6).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.05 * torch.randn(d, generator=gen)).to(torch.bfloat16))
+    return norm
+
+
+class _Bf16Attn(_Attn):
+    """Unquantised projections (no ``forward_quantized``): the bf16 route."""
+
+    def __init__(self, hidden, heads, gen):
+        nn.Module.__init__(self)
+        self.heads = heads
+        self.to_qkv = _bf16_linear(hidden, 3 * hidden, gen)
+        self.to_out = nn.ModuleList([_bf16_linear(hidden, hidden, gen), nn.Dropout(0.0)])
+        self.norm_q, self.norm_k = _Norm(hidden // heads, gen), _Norm(hidden // heads, gen)
+        self.fused_projections = True
+        self.processor = None
+
+
+class _NativeAttn(nn.Module):
+    """Stands in for a native attention module: (x, rotary, mask) -> x W^T + b."""
+
+    def __init__(self, hidden, gen):
+        super().__init__()
+        self.proj = _bf16_linear(hidden, hidden, gen)
+
+    def forward(self, hidden_states, rotary_emb=None, attention_mask=None):
+        return self.proj(hidden_states)
+
+
+class _Bf16Block(_Block):
+    def __init__(self, hidden, heads, inner, gen, native_modules):
+        super().__init__(hidden, heads, inner, gen)
+        if native_modules:
+            self.norm1, self.norm2 = _native_norm(hidden, gen), _native_norm(hidden, gen)
+            self.attn = _NativeAttn(hidden, gen)
+        else:
+            self.attn = _Bf16Attn(hidden, heads, gen)
+        self.ff.net = nn.ModuleList([_Up(_bf16_linear(hidden, 2 * inner, gen)), nn.Dropout(0.0),
+                                     _bf16_linear(inner, hidden, gen)])
+
+
+def _block_inputs(gen, s, hidden, heads, rows=1):
+    x = torch.randn(1, s, hidden, generator=gen).to(torch.bfloat16).to(DEV)
+    temb = torch.randn(rows, hidden, generator=gen).to(torch.bfloat16).to(DEV)
+    idx = torch.randint(0, rows, (s,), generator=gen).to(DEV)
+    phase = torch.randn(s, hidden // heads, generator=gen).to(DEV)
+    return x, temb, idx, (phase.cos(), phase.sin())
+
+
+def test_fused_block_bf16_route():
+    """enable_fusion without quantisation: the bf16 route of
+    model/fusion.py:81-98 (RMSNorm+adaLN kernel, bf16 projections, gated
+    residual, SwiGLU), equal to the kernels called one by one."""
+    gen = torch.Generator().manual_seed(71)
+    hidden, heads, inner, s = 512, 4, 768, 260
+    block = _Bf16Block(hidden, heads, inner, gen, native_modules=False).to(DEV)
+    fusion.enable_fusion(SimpleNamespace(transformer_blocks=[block]))
+    x, temb, idx, rot = _block_inputs(gen, s, hidden, heads, rows=3)
+    with torch.no_grad():
+        got = block.forward(x, temb, idx, rot)
+        lin = block.adaln_proj.linear
+        table = lin(F.silu(temb).to(lin.weight.dtype)).view(-1, 6 * hidden)
+        qkv = block.attn.to_qkv(K._rms_adaln(x, block.norm1, table, idx, 0, 1))
+        q, k, v = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+        qo, ko = K.qk_norm_rope(q, k, block.attn.norm_q, block.attn.norm_k, rot)
+        ao = block.attn.to_out[0](attention_bshd(qo, ko, v).flatten(2, 3).type_as(qo))
+        h = K._gated_residual(x, ao, table, idx, 2)
+        proj = block.ff.net[0].proj(K._rms_adaln(h, block.norm2, table, idx, 3, 4))
+        expect = K._gated_residual(h, block.ff.net[2](K._swiglu(proj)), table, idx, 5)
+    assert torch.equal(got, expect)
+    assert _lib.device_status(clear=True) == 0
+
+
+def test_elementwise_block_matches_reference_composition():
+    """enable_elementwise_fusion: native norms and attention, gated residuals
+    and SwiGLU on the kernels; equal to model/elementwise_fusion.py:7-19
+    written out with table.chunk(6)."""
+    from lynnreal_omni_b200 import elementwise_fusion
+    gen = torch.Generator().manual_seed(72)
+    hidden, heads, inner, s = 512, 4, 768, 301
+    block = _Bf16Block(hidden, heads, inner, gen, native_modules=True).to(DEV).eval()
+    elementwise_fusion.enable_elementwise_fusion(SimpleNamespace(transformer_blocks=[block], training=False))
+    x, temb, idx, rot = _block_inputs(gen, s, hidden, heads, rows=2)
+    with torch.no_grad():
+        got = block.forward(x, temb, idx, rot)
+        lin = block.adaln_proj.linear
+        table = lin(F.silu(temb).to(lin.weight.dtype)).view(-1, 6 * hidden)
+        shift, scale, _, ff_shift, ff_scale, _ = table.chunk(6, dim=-1)
+        n = block.norm1(x) * (1 + scale.index_select(0, idx)) + shift.index_select(0, idx)
+        h = K._gated_residual(x, block.attn(n, rot, None), table, idx, 2)
+        n = block.norm2(h) * (1 + ff_scale.index_select(0, idx)) + ff_shift.index_select(0, idx)
+        update = block.ff.net[2](K._swiglu(block.ff.net[0].proj(n)))
+        expect = K._gated_residual(h, update, table, idx, 5)
+    assert torch.equal(got, expect)
+    assert torch.isfinite(got.float()).all()
+    assert _lib.device_status(clear=True) == 0
