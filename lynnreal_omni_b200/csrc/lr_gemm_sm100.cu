@@ -345,15 +345,17 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
   nb = r / gsize;
 }
 
-// Epilogue of one 32-column chunk of one row, vectorised (all 32 columns valid).
-template <int EPI>
-__device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[32],
+// Epilogue of one W-column chunk of one row (W a multiple of 8), vectorised
+// (all W columns valid).
+template <int EPI, int W = 32>
+__device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[W],
                                                 int64_t row, int col0, float rs,
                                                 const bf16* gate_ptr, bool have_gate) {
+  static_assert(W % 8 == 0, "chunk width");
   const float4* cs4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
-  float d[32];
+  float d[W];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
+  for (int q = 0; q < W / 4; ++q) {
     const float4 c = __ldg(cs4 + q);
     d[4 * q + 0] = dequant((int32_t)acc[4 * q + 0], rs, c.x);
     d[4 * q + 1] = dequant((int32_t)acc[4 * q + 1], rs, c.y);
@@ -363,7 +365,7 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
   if (ep.bias != nullptr) {
     const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + col0);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < W / 8; ++q) {
       float b[8];
       unpack8(__ldg(b4 + q), b);
 #pragma unroll
@@ -372,7 +374,7 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
   }
   uint4* dst = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col0);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < W / 8; ++q) {
     float o[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[e] = d[8 * q + e];
@@ -847,57 +849,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ------------------------------------------------------- split-K finishing
-// Dequantise the summed int32 split-K workspace [M, N] and apply the epilogue:
-// one CTA per row, each thread 32 consecutive columns per step (same epilogue
-// code as the tensor-core kernels, so the bits are the same).
+// Dequantise the summed int32 split-K workspace [M, N] and apply the epilogue
+// (the same epilogue code as the tensor-core kernels, so the bits are the
+// same). Split-K is only taken for outputs that allow 16-byte accesses (N a
+// multiple of 8, aligned workspace): a thread per 8 consecutive columns of
+// one row, so each warp reads 1 KB contiguous runs of every slice's plane.
 template <int EPI>
 __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const int32_t* __restrict__ ws, int M,
-                                                              int N, int splits, const EpiArgs ep,
-                                                              int vec) {
+                                                              int N, int splits, const EpiArgs ep) {
   const int64_t row = blockIdx.x;
+  const int col0 = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (col0 >= N) return;
   const float rs = ep.row_scale[row];
   const bf16* gptr = nullptr;
   bool have_gate = false;
   if (EPI == kGated && ep.table != nullptr) {
     bool bad;
     const bf16* g = gate_row(ep, row, bad);
-    if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+    if (bad && col0 == 0) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
     if (g != nullptr) {
       gptr = g + (int64_t)ep.gate_slot * N;
       have_gate = true;
     }
   }
-  const int64_t plane = (int64_t)M * N;
-  for (int col0 = threadIdx.x * 32; col0 < N; col0 += 256 * 32) {
-    uint32_t acc[32];
-    const int32_t* src = ws + row * (int64_t)N + col0;
-    const bool full = vec && col0 + 32 <= N;
-    // sum the K slices' partial accumulators, slice 0 first (exact int32 adds)
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        int4 sum = __ldcs(reinterpret_cast<const int4*>(src) + q);
-        for (int sp = 1; sp < splits; ++sp) {
-          const int4 v = __ldcs(reinterpret_cast<const int4*>(src + sp * plane) + q);
-          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-        }
-        acc[4 * q] = (uint32_t)sum.x;
-        acc[4 * q + 1] = (uint32_t)sum.y;
-        acc[4 * q + 2] = (uint32_t)sum.z;
-        acc[4 * q + 3] = (uint32_t)sum.w;
-      }
-      store_chunk_vec<EPI>(ep, acc, row, col0, rs, gptr, have_gate);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        int32_t sum = 0;
-        if (col0 + j < N)
-          for (int sp = 0; sp < splits; ++sp) sum += src[sp * plane + j];
-        acc[j] = (uint32_t)sum;
-      }
-      store_chunk_tail<EPI>(ep, acc, row, col0, N, rs, gptr, have_gate);
-    }
+  const int64_t plane4 = (int64_t)M * N / 4;  // one slice's plane, in int4 units
+  const int4* src = reinterpret_cast<const int4*>(ws + row * (int64_t)N + col0);
+  // sum the K slices' partial accumulators, slice 0 first (exact int32 adds)
+  int4 lo = __ldcs(src), hi = __ldcs(src + 1);
+#pragma unroll 4
+  for (int sp = 1; sp < splits; ++sp) {
+    const int4 a = __ldcs(src + sp * plane4), b = __ldcs(src + sp * plane4 + 1);
+    lo.x += a.x; lo.y += a.y; lo.z += a.z; lo.w += a.w;
+    hi.x += b.x; hi.y += b.y; hi.z += b.z; hi.w += b.w;
   }
+  const uint32_t acc[8] = {(uint32_t)lo.x, (uint32_t)lo.y, (uint32_t)lo.z, (uint32_t)lo.w,
+                           (uint32_t)hi.x, (uint32_t)hi.y, (uint32_t)hi.z, (uint32_t)hi.w};
+  store_chunk_vec<EPI, 8>(ep, acc, row, col0, rs, gptr, have_gate);
 }
 
 // ---------------------------------------------------------- CUDA-core path
@@ -1104,8 +1091,10 @@ int launch_tc2_splitk(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb
       ma, mb, M, N, K, raster_group(256, num_m, K), splits, acc);
   st = launch_status("int8 gemm (tcgen05, CTA pair, split-K)");
   if (st) return st;
-  splitk_epilogue_kernel<EPI><<<M, 256, 0, stream>>>(ws, M, N, splits, ep,
-                                                    (vec && N % 4 == 0 && aligned(ws, 16)) ? 1 : 0);
+  if (!vec || N % 8 != 0 || !aligned(ws, 16))
+    return set_error(LR_ERR_UNSUPPORTED, "int8 gemm split-K: output not vectorisable");
+  const dim3 grid((unsigned)M, (unsigned)((N / 8 + 255) / 256));
+  splitk_epilogue_kernel<EPI><<<grid, 256, 0, stream>>>(ws, M, N, splits, ep);
   return launch_status("int8 gemm split-K epilogue");
 }
 
