@@ -54,6 +54,25 @@ const char* lr_last_error(void);
  * kernel's bounded waits. Synchronises the device. */
 int lr_device_status(unsigned int* bits, int clear);
 
+/* Arithmetic of the divisions and RMS reciprocal square roots of the
+ * element-wise kernels (K1, K3, K4, K7, K8 and the Q/K RMSNorm) on the current
+ * device:
+ *   LR_ARITH_REFERENCE_GPU (default): as the reference's Triton kernels
+ *     compile on the GPU (model/kernels.py:13-14, 65, 106, 121-126: fp32 `/`
+ *     is div.full.f32, tl.rsqrt is rsqrt.approx.f32), so the int8
+ *     activations and row scales equal what the reference computes on the
+ *     same GPU;
+ *   LR_ARITH_IEEE: IEEE round-to-nearest division and square root, as the
+ *     reference's PyTorch path (model/int8.py:66-67) and its kernels under
+ *     the Triton interpreter compute them; a CPU restatement reproduces it.
+ * Sums of squares use one order in both modes: the reference's compiled
+ * tl.sum order (8 warps, 8 columns per thread; exact for rows of 2048 or more
+ * columns). Set it before launching work on the device. */
+#define LR_ARITH_IEEE 0
+#define LR_ARITH_REFERENCE_GPU 1
+int lr_set_arithmetic(int mode);
+int lr_get_arithmetic(int* mode);
+
 /* K1 — per-row dynamic int8 quantisation.
  * Replaces model/kernels.py:19-24 `quantize_rows` (kernel :8-16) and the torch
  * quantiser of Int8Linear.forward, model/int8.py:66-67.

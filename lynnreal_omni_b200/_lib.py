@@ -34,6 +34,8 @@ SIGNATURES = {
     "lr_version": ([], _i32),
     "lr_last_error": ([], ctypes.c_char_p),
     "lr_device_status": ([ctypes.POINTER(ctypes.c_uint), _i32], _i32),
+    "lr_set_arithmetic": ([_i32], _i32),
+    "lr_get_arithmetic": ([ctypes.POINTER(ctypes.c_int)], _i32),
     "lr_quantize_rows": ([_p, _i64, _i64, _i64, _p, _p, _p], _i32),
     "lr_int8_epilogue": ([_p, _i64, _i64, _p, _p, _p, _p, _p], _i32),
     "lr_rms_adaln": ([_p, _p, _f32, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _i32, _p, _p], _i32),
@@ -111,6 +113,26 @@ def stream_of(tensor: torch.Tensor) -> int:
     if tensor.device.type != "cuda":
         raise ValueError("the W8A8 ops run on CUDA tensors only")
     return torch.cuda.current_stream(tensor.device).cuda_stream
+
+
+ARITHMETIC = {"reference_gpu": 1, "ieee": 0}
+
+
+def set_arithmetic(mode: str) -> None:
+    """Arithmetic of the element-wise kernels' divisions and RMS reciprocal
+    square roots on the current device: "reference_gpu" (default; as the
+    reference's compiled Triton kernels) or "ieee" (as its PyTorch path and
+    the CPU oracle)."""
+    if mode not in ARITHMETIC:
+        raise ValueError(f"arithmetic must be one of {sorted(ARITHMETIC)}, got {mode!r}")
+    check(load().lr_set_arithmetic(ARITHMETIC[mode]), "set_arithmetic")
+
+
+def arithmetic() -> str:
+    """The current device's arithmetic mode (see set_arithmetic)."""
+    value = ctypes.c_int(0)
+    check(load().lr_get_arithmetic(ctypes.byref(value)), "arithmetic")
+    return {v: k for k, v in ARITHMETIC.items()}[value.value]
 
 
 def device_status(clear: bool = True) -> int:

@@ -5,8 +5,10 @@
 //     matching the reference's `enable_fp_fusion=False` launches
 //     (model/kernels.py:270,287,302; model/int8_gemm.py:243,260);
 //   * bf16 rounding points are round-to-nearest-even;
-//   * divisions and the RMS reciprocal square root are IEEE round-to-nearest
-//     (__fdiv_rn, __fsqrt_rn, __frcp_rn), so a CPU restatement reproduces them;
+//   * divisions and the RMS reciprocal square root either as the reference's
+//     compiled kernels execute them on the GPU (div.full, rsqrt.approx) or
+//     IEEE round-to-nearest (__fdiv_rn, __fsqrt_rn), which a CPU restatement
+//     reproduces (see quotient());
 //   * float -> int8 quantisation rounds half to even.
 //
 // Packed bf16 arithmetic. Where the reference computes an fp32 product or sum
@@ -17,10 +19,11 @@
 // significand bits, so the double rounding is innocuous) — outside the
 // subnormal range, which activations of this path do not reach.
 //
-// Reductions use one fixed tree: per thread two running partials (even and odd
-// columns of its chunks) added at the end, then (block_sum) an xor butterfly
-// inside each warp and a pairwise tree over the warps. The CPU oracle restates
-// the same tree.
+// Reductions use one fixed tree, the one the reference's compiled tl.sum uses
+// for a row of 8 warps with 8 elements per thread (rows of 2048 columns or
+// more): each thread adds its values in order, chunk by chunk, then an xor
+// butterfly (16, 8, 4, 2, 1) inside each warp and an xor butterfly (4, 2, 1)
+// over the warp sums (block_sum). The CPU oracle restates the same tree.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -99,14 +102,41 @@ __device__ __forceinline__ uint32_t bamax8(uint32_t acc, const uint4& a) {
 }
 
 // ------------------------------------------------------------- quantisation
+// Division and the RMS reciprocal square root come in two forms, chosen per
+// launch (`gpu`):
+//   gpu = true   the instructions the reference's Triton kernels compile to on
+//                the GPU: fp32 `/` is PTX div.full.f32 and tl.rsqrt is PTX
+//                rsqrt.approx.f32 (what the reference computes on a B200);
+//   gpu = false  IEEE round-to-nearest (__fdiv_rn, __fsqrt_rn): the
+//                reference's PyTorch path and its Triton kernels under the
+//                Triton interpreter, which the CPU oracle restates.
+__device__ __forceinline__ float div_full(float a, float b) {
+  float d;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float rsqrt_approx(float a) {
+  float d;
+  asm("rsqrt.approx.f32 %0, %1;" : "=f"(d) : "f"(a));
+  return d;
+}
+__device__ __forceinline__ float quotient(float a, float b, bool gpu) {
+  return gpu ? div_full(a, b) : __fdiv_rn(a, b);
+}
+// 1 / sqrt(ss / n + eps)   (model/kernels.py:65,106)
+__device__ __forceinline__ float rms_factor(float ss, float n, float eps, bool gpu) {
+  if (gpu) return rsqrt_approx(__fadd_rn(div_full(ss, n), eps));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, n), eps)));
+}
+
 // Row scale from a row absmax: max(absmax, 1e-8) / 127 (model/kernels.py:13,121-122).
-__device__ __forceinline__ float row_scale_from_absmax(float absmax) {
-  return __fdiv_rn(fmaxf(absmax, 1.0e-8f), 127.0f);
+__device__ __forceinline__ float row_scale_from_absmax(float absmax, bool gpu) {
+  return quotient(fmaxf(absmax, 1.0e-8f), 127.0f, gpu);
 }
 
 // Scalar reference form: RNE(clamp(v / s, -127, 127)) (model/kernels.py:14,126).
-__device__ __forceinline__ int quant_i8(float v, float s) {
-  float q = __fdiv_rn(v, s);
+__device__ __forceinline__ int quant_i8(float v, float s, bool gpu) {
+  float q = quotient(v, s, gpu);
   q = fminf(fmaxf(q, -127.0f), 127.0f);
   return __float2int_rn(q);
 }
@@ -120,11 +150,20 @@ __device__ __forceinline__ int quant_i8(float v, float s) {
 //     2^-14 of a half-integer; those (rare) rows redo the IEEE division;
 //   * rounding to an integer is the float add of 1.5*2^23 (exact RNE for
 //     |q| < 2^22), whose low mantissa byte is the two's-complement int8.
-__device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv) {
+// With `gpu` the quotient is div.full.f32 itself, as the compiled reference
+// forms it (within 2 ulp of v / s, so the clamp still never binds).
+__device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool gpu) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   float f[8];
   unpack8(v, f);
   uint32_t b[8];
+  if (gpu) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(div_full(f[e], s), kMagic));
+    const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+    const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+    return make_uint2(lo, hi);
+  }
   bool near_tie = false;
   const float2 inv2 = make_float2(inv, inv);
   const float2 magic2 = make_float2(kMagic, kMagic);
@@ -170,11 +209,12 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   float s[NWARPS];
 #pragma unroll
   for (int w = 0; w < NWARPS; ++w) s[w] = scratch[w];
-  // pairwise tree: level by level, neighbours (0,1),(2,3),... then (01,23),...
+  // xor butterfly over the warp sums, as warp 0's lanes would run it:
+  // s[w] += s[w ^ off] for off = NWARPS/2, ..., 1; the result is s[0]
 #pragma unroll
-  for (int width = NWARPS; width > 1; width >>= 1) {
+  for (int off = NWARPS / 2; off > 0; off >>= 1) {
 #pragma unroll
-    for (int i = 0; i < width / 2; ++i) s[i] = __fadd_rn(s[2 * i], s[2 * i + 1]);
+    for (int w = 0; w < off; ++w) s[w] = __fadd_rn(s[w], s[w + off]);
   }
   __syncthreads();
   return s[0];

@@ -21,12 +21,14 @@
 #ifndef LR_RMS_MINB
 #define LR_RMS_MINB 4
 #endif
-// The same caps for the two-row residual RMSNorm kernel (K8: 0, a cap measured
-// slower), for the quantiser on rows of more than 4 chunks per thread (K1 on
+// The same caps for the two-row residual RMSNorm kernel on rows of up to 3
+// chunks per thread (K8: 3 -> 80 registers, 3 CTAs per SM; 123 -> 108 us at
+// 12240 x 6144 with the 16-column sum order), for the quantiser on rows of
+// more than 4 chunks per thread (K1 on
 // FFN widths: 4 -> 64 registers; 185 -> 140 us at 12240 x 24576, ~ the HBM copy
 // rate) and for the SwiGLU kernels (4: 292 -> 270 us at 12240 x 2 x 14336).
 #ifndef LR_RMS2_MINB
-#define LR_RMS2_MINB 0
+#define LR_RMS2_MINB 3
 #endif
 #ifndef LR_QUANT_WIDE_MINB
 #define LR_QUANT_WIDE_MINB 4
@@ -47,6 +49,13 @@
 namespace lr {
 
 static __device__ unsigned int g_device_status = 0;
+
+// Arithmetic of divisions and the RMS reciprocal square root for every kernel
+// of this file (see quotient() in lr_common.cuh): 1 = as the reference's
+// compiled Triton kernels on the GPU (the default), 0 = IEEE, as its PyTorch
+// path and the CPU oracle. One value per device, set by lr_set_arithmetic.
+__constant__ int c_arith_gpu = 1;
+__device__ __forceinline__ bool arith_gpu() { return c_arith_gpu != 0; }
 
 __device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_device_status, bits); }
 
@@ -109,13 +118,14 @@ __global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : LR_QUA
 #pragma unroll
     for (int c = 0; c < C; ++c) amax2 = bamax8(amax2, raw[c]);
     const float amax = block_max<kWarps>(bamax_final(amax2), red);
-    const float s = row_scale_from_absmax(amax);
+    const bool gpu = arith_gpu();
+    const float s = row_scale_from_absmax(amax, gpu);
     const float inv = __frcp_rn(s);
     int8_t* dst = q + row * (int64_t)width;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      store_q8<VEC>(dst, col, width, quant8(raw[c], s, inv));
+      store_q8<VEC>(dst, col, width, quant8(raw[c], s, inv, gpu));
     }
     if (threadIdx.x == 0) scales[row] = s;
     if (next >= rows) break;
@@ -130,9 +140,77 @@ __global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : LR_QUA
 }
 
 // --------------------------------------------------------------- K3/K4/K8
+// Sums of squares in the reference's compiled order. Its bf16-output kernel
+// lays a row out with 8 columns per thread, like the chunks here, and each
+// thread adds its squares in column order. Its int8-output kernels lay it out
+// with 16 columns per thread (the 16-byte int8 stores): thread t' adds columns
+// 4096 r + 16 t' + [0, 16) for r = 0, 1, ... . Here thread t holds the 8-column
+// chunks c*256 + t, so the 16-column thread j + 128 p (j = t >> 1, p = 0, 1) is
+// the chain over chunks c = p, p + 2, ... alternating between the lanes 2j
+// and 2j + 1: the running sum crosses the lane pair by shuffles. The 256
+// chains go through `stage` to the thread with their index, so block_sum then
+// reduces them in the reference's butterflies. Squares of bf16 values are
+// exact in fp32, so each fused multiply-add equals the separate multiply and add.
+template <int C>
+__device__ __forceinline__ float sumsq_part8(const uint4 (&v)[C]) {
+  float part = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float f[8];
+    unpack8(v[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part = __fmaf_rn(f[e], f[e], part);
+  }
+  return part;
+}
+
+template <int C>
+__device__ __forceinline__ float sumsq_part16(const uint4 (&v)[C], float* stage) {
+  const int lane = threadIdx.x & 31;
+  float acc[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float f[8];
+    unpack8(v[c], f);
+    float a = acc[c & 1];  // the even lane continues the chain with its chunk
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a = __fmaf_rn(f[e], f[e], a);
+    float b = __shfl_sync(0xffffffffu, a, lane & ~1);  // then the odd lane with its own
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b = __fmaf_rn(f[e], f[e], b);
+    acc[c & 1] = __shfl_sync(0xffffffffu, b, lane | 1);
+  }
+  stage[(threadIdx.x >> 1) + 128 * (threadIdx.x & 1)] = acc[threadIdx.x & 1];
+  __syncthreads();
+  return stage[threadIdx.x];
+}
+
+// Both rows of the two-row kernel at once (.x row 0, .y row 1).
+template <int C>
+__device__ __forceinline__ float2 sumsq_part16x2(const uint4 (&v0)[C], const uint4 (&v1)[C], float2* stage) {
+  const int lane = threadIdx.x & 31;
+  float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float f0[8], f1[8];
+    unpack8(v0[c], f0);
+    unpack8(v1[c], f1);
+    float2 a = acc[c & 1];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a = __ffma2_rn(make_float2(f0[e], f1[e]), make_float2(f0[e], f1[e]), a);
+    float2 b = make_float2(__shfl_sync(0xffffffffu, a.x, lane & ~1), __shfl_sync(0xffffffffu, a.y, lane & ~1));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b = __ffma2_rn(make_float2(f0[e], f1[e]), make_float2(f0[e], f1[e]), b);
+    acc[c & 1] = make_float2(__shfl_sync(0xffffffffu, b.x, lane | 1), __shfl_sync(0xffffffffu, b.y, lane | 1));
+  }
+  stage[(threadIdx.x >> 1) + 128 * (threadIdx.x & 1)] = acc[threadIdx.x & 1];
+  __syncthreads();
+  return stage[threadIdx.x];
+}
+
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
 __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4 (&v)[C],
-                                            const uint4 (&d)[C], float* red) {
+                                            const uint4 (&d)[C], float* red, float* stage) {
   const int hidden = a.hidden;
   bool bad;
   const bf16* trow = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence,
@@ -154,24 +232,12 @@ __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4
     }
   }
 
-  // Sum of squares in the fixed order: two running partials per thread, over
-  // the even and the odd columns of its chunks (chunk by chunk, left to right),
-  // added at the end. A bf16 value's square is exact in fp32, so the fused
-  // multiply-add rounds exactly like the reference's separate multiply and add.
-  float2 part2 = make_float2(0.0f, 0.0f);
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    float f[8];
-    unpack8(v[c], f);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float2 x2 = make_float2(f[e], f[e + 1]);
-      part2 = __ffma2_rn(x2, x2, part2);
-    }
-  }
-  const float ss = block_sum<kWarps>(__fadd_rn(part2.x, part2.y), red);
+  // sum of squares in the order of the reference's kernel for this output
+  const float part = (QUANT && C >= 2) ? sumsq_part16<C>(v, stage) : sumsq_part8<C>(v);
+  const float ss = block_sum<kWarps>(part, red);
   // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hidden), a.eps)));
+  const bool gpu = arith_gpu();
+  const float r = rms_factor(ss, (float)hidden, a.eps, gpu);
 
   uint32_t amax2 = 0u;
 #pragma unroll
@@ -201,13 +267,13 @@ __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4
 
   if (QUANT) {
     const float amax = block_max<kWarps>(bamax_final(amax2), red);
-    const float s = row_scale_from_absmax(amax);
+    const float s = row_scale_from_absmax(amax, gpu);
     const float inv = __frcp_rn(s);
     int8_t* dst = a.q + row * (int64_t)hidden;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-      store_q8<VEC>(dst, col, hidden, quant8(v[c], s, inv));
+      store_q8<VEC>(dst, col, hidden, quant8(v[c], s, inv, gpu));
     }
     if (threadIdx.x == 0) a.scales[row] = s;
   } else {
@@ -222,6 +288,7 @@ __device__ __forceinline__ void rms_mod_row(const RmsArgs& a, int64_t row, uint4
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
 __global__ void __launch_bounds__(kThreads, (C <= 4 ? LR_RMS_MINB : 0)) rms_mod_kernel(const RmsArgs a) {
   __shared__ float red[kWarps];
+  __shared__ float stage[(QUANT && C >= 2) ? kThreads : 1];
   constexpr bool kPre = Prefetch<C>::kOn;
   constexpr int kN = Prefetch<C>::kN;
   constexpr int kD = RESID ? C : 1;
@@ -240,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, (C <= 4 ? LR_RMS_MINB : 0)) rms_mod_
     uint4 dd[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) dd[c] = d[RESID ? c : 0];
-    rms_mod_row<C, VEC, RESID, MOD, QUANT>(a, row, v, dd, red);
+    rms_mod_row<C, VEC, RESID, MOD, QUANT>(a, row, v, dd, red, stage);
     if (next >= a.rows) break;
     if (kPre) {
 #pragma unroll
@@ -275,10 +342,9 @@ __device__ __forceinline__ float2 block_sum2(float2 v, float2* scratch) {
 #pragma unroll
   for (int w = 0; w < NWARPS; ++w) s[w] = scratch[w];
 #pragma unroll
-  for (int width = NWARPS; width > 1; width >>= 1) {
+  for (int off = NWARPS / 2; off > 0; off >>= 1) {
 #pragma unroll
-    for (int i = 0; i < width / 2; ++i)
-      s[i] = make_float2(__fadd_rn(s[2 * i].x, s[2 * i + 1].x), __fadd_rn(s[2 * i].y, s[2 * i + 1].y));
+    for (int w = 0; w < off; ++w) s[w] = make_float2(__fadd_rn(s[w].x, s[w + off].x), __fadd_rn(s[w].y, s[w + off].y));
   }
   __syncthreads();
   return s[0];
@@ -302,8 +368,9 @@ __device__ __forceinline__ float2 block_max2(float2 v, float2* scratch) {
 }
 
 template <int C, bool VEC, bool RESID, bool MOD, bool QUANT>
-__global__ void __launch_bounds__(kThreads, LR_RMS2_MINB) rms_mod2_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreads, (C <= 3 ? LR_RMS2_MINB : 0)) rms_mod2_kernel(const RmsArgs a) {
   __shared__ float2 red[kWarps];
+  __shared__ float2 stage[(QUANT && C >= 2) ? kThreads : 1];
   const int hidden = a.hidden;
   const int64_t row0 = 2 * (int64_t)blockIdx.x;
   const bool has1 = row0 + 1 < a.rows;
@@ -344,27 +411,26 @@ __global__ void __launch_bounds__(kThreads, LR_RMS2_MINB) rms_mod2_kernel(const 
         if (j == 0 || has1) store_chunk<VEC>(a.residual_out + rows2[j] * (int64_t)hidden, col, hidden, v[j][c]);
       }
   }
-  // sum of squares per row: two running partials per thread (even / odd columns)
-  float part[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    float2 p2 = make_float2(0.0f, 0.0f);
+  // sums of squares of both rows (.x row 0, .y row 1) in the order of the
+  // reference's kernel for this output
+  float2 part;
+  if (QUANT && C >= 2) {
+    part = sumsq_part16x2<C>(v[0], v[1], stage);
+  } else {
+    part = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      float f[8];
-      unpack8(v[j][c], f);
+      float f0[8], f1[8];
+      unpack8(v[0][c], f0);
+      unpack8(v[1][c], f1);
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const float2 x2 = make_float2(f[e], f[e + 1]);
-        p2 = __ffma2_rn(x2, x2, p2);
-      }
+      for (int e = 0; e < 8; ++e) part = __ffma2_rn(make_float2(f0[e], f1[e]), make_float2(f0[e], f1[e]), part);
     }
-    part[j] = __fadd_rn(p2.x, p2.y);
   }
-  const float2 ss = block_sum2<kWarps>(make_float2(part[0], part[1]), red);
+  const float2 ss = block_sum2<kWarps>(part, red);
   // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
-  const float rr[2] = {__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss.x, (float)hidden), a.eps))),
-                       __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss.y, (float)hidden), a.eps)))};
+  const bool gpu = arith_gpu();
+  const float rr[2] = {rms_factor(ss.x, (float)hidden, a.eps, gpu), rms_factor(ss.y, (float)hidden, a.eps, gpu)};
   uint32_t amax2[2] = {0u, 0u};
 #pragma unroll
   for (int c = 0; c < C; ++c) {
@@ -400,12 +466,12 @@ __global__ void __launch_bounds__(kThreads, LR_RMS2_MINB) rms_mod2_kernel(const 
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       if (j == 1 && !has1) break;
-      const float s = row_scale_from_absmax(am[j]);
+      const float s = row_scale_from_absmax(am[j], gpu);
       const float inv = __frcp_rn(s);
       int8_t* dst = a.q + rows2[j] * (int64_t)hidden;
 #pragma unroll
       for (int c = 0; c < C; ++c)
-        store_q8<VEC>(dst, ((int64_t)c * kThreads + threadIdx.x) * 8, hidden, quant8(v[j][c], s, inv));
+        store_q8<VEC>(dst, ((int64_t)c * kThreads + threadIdx.x) * 8, hidden, quant8(v[j][c], s, inv, gpu));
       if (threadIdx.x == 0) a.scales[rows2[j]] = s;
     }
   } else {
@@ -508,13 +574,14 @@ __global__ void __launch_bounds__(kThreads, LR_SWIGLU_MINB) swiglu_kernel(const 
     }
     if (QUANT) {
       const float amax = block_max<kWarps>(bamax_final(amax2), red);
-      const float s = row_scale_from_absmax(amax);
+      const bool gpu = arith_gpu();
+      const float s = row_scale_from_absmax(amax, gpu);
       const float inv = __frcp_rn(s);
       int8_t* dst = q + row * (int64_t)inner;
 #pragma unroll
       for (int c = 0; c < C; ++c) {
         const int64_t col = ((int64_t)c * kThreads + threadIdx.x) * 8;
-        store_q8<VEC>(dst, col, inner, quant8(v[c], s, inv));
+        store_q8<VEC>(dst, col, inner, quant8(v[c], s, inv, gpu));
       }
       if (threadIdx.x == 0) scales[row] = s;
     } else {
@@ -594,7 +661,7 @@ __global__ void __launch_bounds__(256, LR_QK_MINB) qk_norm_rope_tok_kernel(
     }
     float ss = __fadd_rn(part.x, part.y);
     for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)head_dim), eps)));
+    const float r = rms_factor(ss, (float)head_dim, eps, arith_gpu());
     const float2 r2 = make_float2(r, r);
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
@@ -654,7 +721,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_row_kernel(
       }
       float ss = __fadd_rn(ev, od);
       for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)head_dim), eps)));
+      const float r = rms_factor(ss, (float)head_dim, eps, arith_gpu());
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int d = lane * 8 + e;
@@ -789,6 +856,20 @@ using lr::bf16;
 using lr::kMaxRows;
 using lr::pick_chunks;
 
+extern "C" int lr_set_arithmetic(int mode) {
+  LR_REQUIRE(mode == LR_ARITH_IEEE || mode == LR_ARITH_REFERENCE_GPU, "set_arithmetic: unknown mode %d", mode);
+  if (cudaMemcpyToSymbol(lr::c_arith_gpu, &mode, sizeof(mode)) != cudaSuccess)
+    return lr::launch_status("setting the arithmetic mode");
+  return LR_OK;
+}
+
+extern "C" int lr_get_arithmetic(int* mode) {
+  LR_REQUIRE(mode != nullptr, "get_arithmetic: null pointer");
+  if (cudaMemcpyFromSymbol(mode, lr::c_arith_gpu, sizeof(int)) != cudaSuccess)
+    return lr::launch_status("reading the arithmetic mode");
+  return LR_OK;
+}
+
 extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
                                 int8_t* q, float* scales, void* stream) {
   LR_REQUIRE(rows >= 0 && width > 0, "quantize_rows: invalid shape [%lld, %lld]", (long long)rows,
@@ -856,6 +937,10 @@ bool vec_ok(int64_t hidden, std::initializer_list<const void*> ptrs) {
 
 }  // namespace
 
+#ifndef LR_RMS2_OFF
+#define LR_RMS2_OFF 0  // 1: the residual variant runs the one-row kernel too (tuning knob)
+#endif
+
 static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, bool quant, bool vec,
                       cudaStream_t s) {
   const int C = pick_chunks(a.hidden);
@@ -864,7 +949,7 @@ static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, 
 // per CTA (measured faster); every other case the persistent one-row kernel.
 // Both reduce each row in the same tree, so their results are identical.
 #define LR_RMS(V, R, M, Q)                                                                        \
-  if (R && kC <= 4)                                                                               \
+  if (R && kC <= 4 && !LR_RMS2_OFF)                                                               \
     lr::rms_mod2_kernel<(kC <= 4 ? kC : 4), V, R, M, Q><<<(unsigned)((rows + 1) / 2), lr::kThreads, 0, s>>>(a); \
   else                                                                                            \
     lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(a)

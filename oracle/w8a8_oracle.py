@@ -15,9 +15,16 @@ are relative to the reference project root) as plain CPU arithmetic:
 Reduction order. The only order-dependent quantity on the path is the
 RMSNorm sum of squares. ``sumsq_numpy`` is the order of the reference's Triton
 kernel when run by the Triton interpreter (``np.sum``); ``sumsq_tree`` is the
-fixed tree of the CUDA kernels (256 threads x 8-column chunks, then a warp
-butterfly, then a pairwise tree over 8 warps). All other steps are
+fixed tree of the CUDA kernels (256 threads x 8-column chunks added in order,
+then a warp butterfly, then a butterfly over the 8 warps), which is also the
+order of the reference's kernel compiled for the GPU. All other steps are
 order-independent.
+
+Division and square root are IEEE round-to-nearest here, as in the
+reference's PyTorch path and under the Triton interpreter. The CUDA kernels
+compute them that way in their "ieee" arithmetic mode; their default mode uses
+the approximate instructions the reference's kernels compile to on the GPU,
+which no CPU restatement reproduces bit for bit.
 
 Parity pinning: ``tests/test_oracle_golden.py`` checks every function here
 against golden vectors produced by the reference itself
@@ -148,38 +155,62 @@ def sumsq_numpy(v: np.ndarray) -> np.ndarray:
     return np.sum(padded * padded, axis=-1, dtype=F32)
 
 
-def sumsq_tree(v: np.ndarray, threads: int = 256) -> np.ndarray:
-    """Row sum of squares in the CUDA kernels' fixed order.
-
-    Thread t owns columns (c*threads + t)*8 + e (chunk c, element e) and keeps
-    two running sums of squares: over the even and over the odd e, chunk by
-    chunk; it adds the two at the end. The 32 lanes of a warp then add by an
-    xor butterfly (16, 8, 4, 2, 1); the warp sums are added pairwise,
-    neighbours first.
-    """
+def _thread_sums(v: np.ndarray, threads: int, per_thread: int) -> np.ndarray:
+    """[rows, threads] sums of squares: thread t adds the squares of columns
+    (r*threads + t)*per_thread + e, e = 0..per_thread-1, r = 0, 1, ... in order."""
     v = np.asarray(v, F32)
     rows, width = v.shape
-    span = threads * 8
-    chunks = max(1, -(-width // span))
-    padded = np.zeros((rows, chunks * span), F32)
+    span = threads * per_thread
+    reps = max(1, -(-width // span))
+    padded = np.zeros((rows, reps * span), F32)
     padded[:, :width] = v
-    sq = (padded * padded).reshape(rows, chunks, threads, 8)
-    even = np.zeros((rows, threads), F32)
-    odd = np.zeros((rows, threads), F32)
-    for c in range(chunks):
-        for e in range(0, 8, 2):
-            even = even + sq[:, c, :, e]
-            odd = odd + sq[:, c, :, e + 1]
-    part = even + odd
+    sq = (padded * padded).reshape(rows, reps, threads, per_thread)
+    part = np.zeros((rows, threads), F32)
+    for r in range(reps):
+        for e in range(per_thread):
+            part = part + sq[:, r, :, e]
+    return part
+
+
+def _butterflies(part: np.ndarray) -> np.ndarray:
+    """An xor butterfly (16, 8, 4, 2, 1) over the 32 lanes of each warp, then
+    one over the warp sums as the lanes of one warp would run it
+    (8 warps: ((w0 + w4) + (w2 + w6)) + ((w1 + w5) + (w3 + w7)))."""
+    rows, threads = part.shape
     warps = threads // 32
     lanes = part.reshape(rows, warps, 32)
     idx = np.arange(32)
     for off in (16, 8, 4, 2, 1):
         lanes = lanes + lanes[:, :, idx ^ off]
     s = lanes[:, :, 0]
-    while s.shape[1] > 1:
-        s = s[:, 0::2] + s[:, 1::2]
+    off = warps // 2
+    while off:
+        s = s[:, :off] + s[:, off:2 * off]
+        off //= 2
     return s[:, 0]
+
+
+def sumsq_tree(v: np.ndarray, threads: int = 256) -> np.ndarray:
+    """Row sum of squares in the order of the CUDA kernels with bf16 output
+    (K3), which is the order of the reference's compiled ``tl.sum`` in its
+    bf16-output kernel (model/kernels.py:65; 8 warps, 8 columns per thread
+    from the 16-byte bf16 accesses) for rows of 2048 columns or more: each
+    thread adds its columns in order, then ``_butterflies``."""
+    return _butterflies(_thread_sums(v, threads, 8))
+
+
+def sumsq_tree16(v: np.ndarray, threads: int = 256) -> np.ndarray:
+    """Row sum of squares in the order of the reference's compiled int8-output
+    kernels (model/kernels.py:106; their 16-byte int8 stores lay a row out
+    with 16 columns per thread: thread t adds columns 4096 r + 16 t + e in
+    order), then ``_butterflies``; the CUDA K4/K8 kernels reproduce it."""
+    return _butterflies(_thread_sums(v, threads, 16))
+
+
+def sumsq_quant(v: np.ndarray) -> np.ndarray:
+    """The order of the int8-output RMSNorm kernels: 16 columns per thread for
+    rows of more than 2048 columns (a 4096-column block or larger), else 8."""
+    return sumsq_tree16(v) if np.asarray(v).shape[-1] > 2048 else sumsq_tree(v)
 
 
 # --------------------------------------------------- K3 / K4 / K8 row kernels
@@ -216,7 +247,7 @@ def rms_adaln(x, weight, eps, table, indices, shift_slot, scale_slot, sequence=N
 
 
 def rms_adaln_quant_int8(x, weight, eps, table, indices, shift_slot, scale_slot, sequence=None,
-                         reduce=sumsq_tree):
+                         reduce=sumsq_quant):
     """RMSNorm + adaLN modulate + per-row int8 quantisation
     (model/kernels.py:81-128, 275-289). Returns (int8, float32 [rows, 1])."""
     m = rms_adaln(x, weight, eps, table, indices, shift_slot, scale_slot, sequence, reduce)
@@ -236,7 +267,7 @@ def gated_residual(x, y, table, indices, gate_slot, sequence=None) -> np.ndarray
     return bf16_round(x + bf16_round(gate * y))
 
 
-def residual_rms_quant(x, update, weight, eps, table, indices, sequence=None, reduce=sumsq_tree):
+def residual_rms_quant(x, update, weight, eps, table, indices, sequence=None, reduce=sumsq_quant):
     """Gated residual (slot 2) fused into the FFN prologue (slots 3, 4)
     (model/kernels.py:101-105, 405-419). Returns (residual, int8, float32 [rows,1])."""
     residual = gated_residual(x, update, table, indices, 2, sequence)

@@ -44,29 +44,43 @@ def gelu_tanh_bf16(x: torch.Tensor) -> torch.Tensor:
     return F.gelu(x.to(BF16), approximate="tanh").to(F32)
 
 
-def sumsq_tree(v: torch.Tensor, threads: int = 256) -> torch.Tensor:
-    """Row sum of squares in the CUDA kernels' order (see w8a8_oracle.sumsq_tree)."""
+def _thread_sums(v: torch.Tensor, threads: int, per_thread: int) -> torch.Tensor:
     rows, width = v.shape
-    span = threads * 8
-    chunks = max(1, -(-width // span))
-    padded = torch.zeros(rows, chunks * span, dtype=F32)
+    span = threads * per_thread
+    reps = max(1, -(-width // span))
+    padded = torch.zeros(rows, reps * span, dtype=F32)
     padded[:, :width] = v
-    sq = (padded * padded).view(rows, chunks, threads, 8)
-    even = torch.zeros(rows, threads, dtype=F32)
-    odd = torch.zeros(rows, threads, dtype=F32)
-    for c in range(chunks):
-        for e in range(0, 8, 2):
-            even = even + sq[:, c, :, e]
-            odd = odd + sq[:, c, :, e + 1]
-    part = even + odd
-    lanes = part.view(rows, threads // 32, 32)
+    sq = (padded * padded).view(rows, reps, threads, per_thread)
+    part = torch.zeros(rows, threads, dtype=F32)
+    for r in range(reps):
+        for e in range(per_thread):
+            part = part + sq[:, r, :, e]
+    return part
+
+
+def _butterflies(part: torch.Tensor) -> torch.Tensor:
+    rows, threads = part.shape
+    warps = threads // 32
+    lanes = part.view(rows, warps, 32)
     idx = torch.arange(32)
     for off in (16, 8, 4, 2, 1):
         lanes = lanes + lanes[:, :, idx ^ off]
     s = lanes[:, :, 0]
-    while s.shape[1] > 1:
-        s = s[:, 0::2] + s[:, 1::2]
+    off = warps // 2
+    while off:
+        s = s[:, :off] + s[:, off:2 * off]
+        off //= 2
     return s[:, 0]
+
+
+def sumsq_tree(v: torch.Tensor, threads: int = 256) -> torch.Tensor:
+    """Row sum of squares in the bf16-output kernels' order (see w8a8_oracle.sumsq_tree)."""
+    return _butterflies(_thread_sums(v, threads, 8))
+
+
+def sumsq_quant(v: torch.Tensor) -> torch.Tensor:
+    """The int8-output kernels' order (see w8a8_oracle.sumsq_quant)."""
+    return _butterflies(_thread_sums(v, 256, 16 if v.shape[-1] > 2048 else 8))
 
 
 def rms_adaln(x, weight, eps, table=None, indices=None, shift_slot=0, scale_slot=1, sequence=None,
@@ -96,7 +110,7 @@ def gated_residual(x, y, table=None, indices=None, gate_slot=0, sequence=None):
     return bf(x + bf(gate * y))
 
 
-def flash_block(x, table, indices, context, w, reduce=sumsq_tree):
+def flash_block(x, table, indices, context, w, reduce=sumsq_quant):
     """The benchmark block's W8A8 path (lynnreal_omni_b200/block.py) on the CPU.
 
     x: bf16/fp32 [M, D]; w: a BlockWeights on the CPU. Returns (x' float32
