@@ -14,6 +14,7 @@ not installed.
 """
 from __future__ import annotations
 
+import json
 import sys
 import warnings
 from pathlib import Path
@@ -119,3 +120,28 @@ def test_ieee_mode_differs_only_in_rounding(ref):
         _lib.set_arithmetic("reference_gpu")
     step = (default[0].int() - ieee[0].int()).abs()
     assert int(step.max()) <= 1 and float((step != 0).float().mean()) < 1e-3
+
+
+def test_outputs_equal_the_recorded_reference_outputs():
+    """Same comparison without the installed reference: SHA-256 digests of the
+    reference's compiled kernels' outputs on a B200, recorded by
+    tests/golden/make_reference_gpu.py on seeded inputs it regenerates."""
+    path = Path(__file__).resolve().parent / "golden" / "reference_gpu.json"
+    if not path.exists():
+        pytest.skip("no recorded reference outputs")
+    sys.path.insert(0, str(path.parent))
+    try:
+        import make_reference_gpu as R
+    finally:
+        sys.path.remove(str(path.parent))
+    record = json.loads(path.read_text())
+    assert _lib.arithmetic() == "reference_gpu"
+    checked = 0
+    for name, case in record["cases"].items():
+        inp = R.reference_gpu_inputs(case["rows"], case["width"], case["seed"], DEV)
+        ours = R.outputs(K, name.split("_")[0], inp)
+        for key, digests in case["sha256"].items():
+            got = [R.digest(t) for t in ours[key]]
+            assert got == digests, (name, key)
+            checked += len(digests)
+    assert checked >= 30
