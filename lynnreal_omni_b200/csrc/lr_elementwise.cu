@@ -610,6 +610,75 @@ __global__ void __launch_bounds__(kThreads, LR_SWIGLU_MINB) swiglu_kernel(const 
 // touches (256 is a multiple of L), so its weights and cos/sin are loaded once
 // per token; the rotary partner chunk is lane p ^ (rotary_dim / 16) of the
 // same head. All NI chunk loads of a thread are issued before any compute.
+// A reduction as a layout of threads holding S consecutive terms each runs it:
+// each thread adds its terms in order, then xor butterflies over the
+// 32-thread warps and over the warps. `t` are this lane's 8 consecutive terms;
+// the head's terms span `lanes` lanes (a power of two).
+template <int S>
+__device__ __forceinline__ float spt_sum(const float (&t)[8], int lanes) {
+  constexpr int J = 8 / S;  // emulated threads per lane
+  float v[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    float acc = t[j * S];
+#pragma unroll
+    for (int e = 1; e < S; ++e) acc = __fadd_rn(acc, t[j * S + e]);
+    v[j] = acc;
+  }
+  const int n = lanes * J;
+  const int wt = n < 32 ? n : 32;
+  for (int off = wt >> 1; off > 0; off >>= 1) {
+    if (off >= J) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], off / J));
+    } else {
+      float w[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) w[j] = __fadd_rn(v[j], v[j ^ off]);
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = w[j];
+    }
+  }
+  for (int off = (n / 32) >> 1; off > 0; off >>= 1) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], off * 32 / J));
+  }
+  return v[0];
+}
+
+// Head-row sum of squares of the Q/K kernels in the order of the reference's
+// compiled Q/K kernels (4 warps, one term per thread, so exact for head
+// dimensions up to 128). `f` are this lane's 8 values (columns 8p .. 8p+7 of
+// the head row), `raw` the same as packed bf16; the head's lanes start at
+// `base`.
+//   * full rotary (paired): terms x_i^2 + x_{i+D/2}^2 for i < D/2
+//     (model/kernels.py:217-222), the partner values from lane p + D/16;
+//   * otherwise: terms x_i^2 (model/kernels.py:374-375).
+// A bf16 value's square is exact in fp32, so a fused multiply-add of one
+// equals the separate multiply and add.
+__device__ __forceinline__ float qk_sumsq(const float (&f)[8], const uint4& raw, int p, int base, int lanes,
+                                          int head_dim, bool paired) {
+  float t[8];
+  int n_lanes = lanes;
+  if (paired) {
+    const int h8 = head_dim >> 4;
+    const int src = base + (p < h8 ? p + h8 : p - h8);
+    const uint4 y = make_uint4(__shfl_sync(0xffffffffu, raw.x, src), __shfl_sync(0xffffffffu, raw.y, src),
+                               __shfl_sync(0xffffffffu, raw.z, src), __shfl_sync(0xffffffffu, raw.w, src));
+    float g[8];
+    unpack8(y, g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = p < h8 ? __fmaf_rn(g[e], g[e], __fmul_rn(f[e], f[e])) : 0.0f;
+    n_lanes = 1;
+    while (n_lanes < h8) n_lanes <<= 1;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = __fmul_rn(f[e], f[e]);
+  }
+  const float total = spt_sum<1>(t, n_lanes);
+  return __shfl_sync(0xffffffffu, total, base);
+}
+
 template <int NI>
 __global__ void __launch_bounds__(256, LR_QK_MINB) qk_norm_rope_tok_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, int64_t q_ts, int64_t k_ts,
@@ -638,6 +707,7 @@ __global__ void __launch_bounds__(256, LR_QK_MINB) qk_norm_rope_tok_kernel(
   unpack8(ld_keep(wk + p * 8), wkf);
   const bool rotates = p * 8 < rotary_dim;
   const bool lower = p * 8 < rotary_dim / 2;
+  const bool paired = rotary_dim == head_dim && head_dim % 16 == 0;
   const int pair = rotary_dim / 16;
   uint4 c2 = make_uint4(0u, 0u, 0u, 0u), s2 = c2;
   if (rotates) {
@@ -653,14 +723,7 @@ __global__ void __launch_bounds__(256, LR_QK_MINB) qk_norm_rope_tok_kernel(
     const bool is_k = c >= qc;
     float f[8];
     unpack8(x[i], f);
-    float2 part = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float2 v2 = make_float2(f[e], f[e + 1]);
-      part = __ffma2_rn(v2, v2, part);  // squares of bf16 values are exact
-    }
-    float ss = __fadd_rn(part.x, part.y);
-    for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+    const float ss = qk_sumsq(f, x[i], p, (t & 31) & ~(lanes - 1), lanes, head_dim, paired);
     const float r = rms_factor(ss, (float)head_dim, eps, arith_gpu());
     const float2 r2 = make_float2(r, r);
 #pragma unroll
@@ -699,6 +762,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_row_kernel(
   __shared__ float buf[8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = rotary_dim / 2;
+  const bool paired = rotary_dim == head_dim && head_dim % 16 == 0;
   const uint16_t* wbits[2] = {reinterpret_cast<const uint16_t*>(wq), reinterpret_cast<const uint16_t*>(wk)};
   for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += (int64_t)gridDim.x * 8) {
     const int64_t token = (row / heads) % sequence;
@@ -711,16 +775,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_row_kernel(
                             token * ts + head * hs;
       uint16_t* dst = reinterpret_cast<uint16_t*>(which ? k_out : q_out) + row * (int64_t)head_dim;
       float x[8];
-      float ev = 0.0f, od = 0.0f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int d = lane * 8 + e;
         x[e] = d < head_dim ? bf_bits(src[d]) : 0.0f;
-        if (e & 1) od = __fmaf_rn(x[e], x[e], od);  // exact square of a bf16 value
-        else ev = __fmaf_rn(x[e], x[e], ev);
       }
-      float ss = __fadd_rn(ev, od);
-      for (int off = lanes >> 1; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+      const uint4 raw = pack8(x);  // exact: the values are bf16
+      const float ss = qk_sumsq(x, raw, lane, 0, lanes, head_dim, paired);
       const float r = rms_factor(ss, (float)head_dim, eps, arith_gpu());
 #pragma unroll
       for (int e = 0; e < 8; ++e) {

@@ -300,27 +300,42 @@ def swiglu_quant_int8(projected):
 # --------------------------------------------- Q/K RMSNorm + RoPE (next row)
 
 
-def sumsq_chunk8(v: np.ndarray) -> np.ndarray:
-    """Row sum of squares in the order of the CUDA Q/K kernels: with
-    L = next power of two >= ceil(width / 8) lanes per head row, lane l holds
-    elements [8l, 8l + 8) and sums the squares of its even and of its odd
-    elements separately, left to right, then adds the two; the L lanes then add
-    by an xor butterfly (L/2, ..., 2, 1). Missing elements count as zero."""
+def _thread_butterflies(terms: np.ndarray) -> np.ndarray:
+    """One term per thread over next_pow2(n) threads (missing terms zero): an
+    xor butterfly over each 32-thread warp, then one over the warp sums."""
+    rows, n = terms.shape
+    block = 1 << max(0, (n - 1).bit_length())
+    padded = np.zeros((rows, block), F32)
+    padded[:, :n] = terms
+    wt = min(32, block)
+    lanes = padded.reshape(rows, block // wt, wt)
+    idx = np.arange(wt)
+    off = wt // 2
+    while off:
+        lanes = lanes + lanes[:, :, idx ^ off]
+        off //= 2
+    s = lanes[:, :, 0]
+    off = s.shape[1] // 2
+    while off:
+        s = s[:, :off] + s[:, off:2 * off]
+        off //= 2
+    return s[:, 0]
+
+
+def sumsq_qk(v: np.ndarray, rotary_dim: int) -> np.ndarray:
+    """Head-row sum of squares in the order of the CUDA Q/K kernels, which is
+    the order of the reference's compiled Q/K kernels (4 warps, one term per
+    thread; exact for head dimensions up to 128):
+      * full rotary (rotary_dim == width, width a multiple of 16), the paired
+        kernel (model/kernels.py:217-222): terms x_i^2 + x_{i+width/2}^2 for
+        i < width/2;
+      * otherwise (model/kernels.py:374-375): terms x_i^2."""
     v = np.asarray(v, F32)
     rows, width = v.shape
-    lanes = 1 << max(0, (-(-width // 8) - 1).bit_length())
-    padded = np.zeros((rows, lanes * 8), F32)
-    padded[:, :width] = v
-    sq = (padded * padded).reshape(rows, lanes, 8)
-    even = ((sq[:, :, 0] + sq[:, :, 2]) + sq[:, :, 4]) + sq[:, :, 6]
-    odd = ((sq[:, :, 1] + sq[:, :, 3]) + sq[:, :, 5]) + sq[:, :, 7]
-    acc = even + odd
-    idx = np.arange(lanes)
-    off = lanes // 2
-    while off:
-        acc = acc + acc[:, idx ^ off]
-        off //= 2
-    return acc[:, 0]
+    if rotary_dim == width and width % 16 == 0:
+        half = width // 2
+        return _thread_butterflies(v[:, :half] * v[:, :half] + v[:, half:] * v[:, half:])
+    return _thread_butterflies(v * v)
 
 
 def sumsq_qk_reference(v: np.ndarray, rotary_dim: int, ordered: bool) -> np.ndarray:
@@ -346,7 +361,7 @@ def sumsq_qk_reference(v: np.ndarray, rotary_dim: int, ordered: bool) -> np.ndar
     return np.sum(padded * padded, axis=-1, dtype=F32)
 
 
-def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=sumsq_chunk8):
+def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=None):
     """Per-head RMSNorm + rotary embedding of one of Q or K
     (model/kernels.py:188-257 full rotary, :345-402 general).
 
@@ -360,7 +375,7 @@ def qk_norm_rope(x, weight, eps, cos, sin, rotary_dim, tokens, reduce=sumsq_chun
     """
     v = np.asarray(x, F32)
     rows, width = v.shape
-    ss = reduce(v)
+    ss = sumsq_qk(v, rotary_dim) if reduce is None else reduce(v)
     r = (F32(1) / np.sqrt(ss / F32(width) + F32(eps))).astype(F32)
     n = bf16_round((v * r[:, None]) * np.asarray(weight, F32)[None, :])
     out = n.copy()

@@ -31,6 +31,11 @@ CASES = [  # (name, rows, width, seed)
     ("swiglu_14336", 48, 14336, 15),
     ("swiglu_2688", 40, 2688, 16),
 ]
+QK_CASES = [  # (name, tokens, heads, head_dim, rotary_dim, seed)
+    ("qk_128_full", 64, 8, 128, 128, 21),
+    ("qk_128_partial", 64, 8, 128, 64, 22),
+    ("qk_96_full", 48, 4, 96, 96, 23),
+]
 
 
 def reference_gpu_inputs(rows: int, width: int, seed: int, device):
@@ -45,6 +50,40 @@ def reference_gpu_inputs(rows: int, width: int, seed: int, device):
     to = lambda t: t.to(device)  # noqa: E731
     return SimpleNamespace(x=to(x), y=to(y), norm=SimpleNamespace(weight=to(weight), eps=1e-6), table=to(table),
                            idx=to(idx), proj=to(proj))
+
+
+def qk_inputs(tokens: int, heads: int, head_dim: int, rotary_dim: int, seed: int, device):
+    """Seeded CPU inputs of one Q/K case: Q and K as strided views of a fused
+    QKV output, norm modules and the rotary tables."""
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(1, tokens, 3 * heads * head_dim, generator=g).to(torch.bfloat16).to(device)
+    q, k, _ = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+    norms = [SimpleNamespace(weight=(1 + 0.05 * torch.randn(head_dim, generator=g)).to(torch.bfloat16).to(device),
+                             eps=1e-6) for _ in range(2)]
+    phase = torch.randn(tokens, rotary_dim, generator=g)
+    return SimpleNamespace(q=q, k=k, norm_q=norms[0], norm_k=norms[1], cos=phase.cos().to(device),
+                           sin=phase.sin().to(device))
+
+
+def reference_qk(rk, inp):
+    """The reference's Q/K kernels launched as its FusedAttention does
+    (model/fusion.py:29-54; on B200 without the ordered reduction)."""
+    import triton
+    q, k = inp.q, inp.k
+    _, s, h, d = q.shape
+    rot = inp.cos.shape[-1]
+    q_out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    k_out = torch.empty_like(k, memory_format=torch.contiguous_format)
+    common = (q, k, inp.norm_q.weight, inp.norm_k.weight, inp.cos, inp.sin, q_out, k_out, s, h, q.stride(1),
+              q.stride(2), k.stride(1), k.stride(2), d)
+    grid = (q.numel() // d,)
+    if rot == d:
+        rk._qk_norm_full_rope_paired_kernel[grid](*common, float(inp.norm_q.eps), triton.next_power_of_2(d // 2),
+                                                 num_warps=4, enable_fp_fusion=False)
+    else:
+        rk._qk_norm_rope_kernel[grid](*common, rot, float(inp.norm_q.eps), triton.next_power_of_2(d),
+                                      num_warps=4, enable_fp_fusion=False)
+    return q_out, k_out
 
 
 def digest(t: torch.Tensor) -> str:
@@ -78,6 +117,11 @@ def main(out_path: str) -> None:
         res = outputs(rk, name.split("_")[0], inp)
         record["cases"][name] = {"rows": rows, "width": width, "seed": seed,
                                  "sha256": {k: [digest(t) for t in v] for k, v in res.items()}}
+    record["qk"] = {}
+    for name, tokens, heads, head_dim, rot, seed in QK_CASES:
+        out = reference_qk(rk, qk_inputs(tokens, heads, head_dim, rot, seed, "cuda"))
+        record["qk"][name] = {"tokens": tokens, "heads": heads, "head_dim": head_dim, "rotary_dim": rot,
+                              "seed": seed, "sha256": [digest(t) for t in out]}
     Path(out_path).write_text(json.dumps(record, indent=1) + "\n")
 
 

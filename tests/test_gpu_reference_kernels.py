@@ -144,4 +144,40 @@ def test_outputs_equal_the_recorded_reference_outputs():
             got = [R.digest(t) for t in ours[key]]
             assert got == digests, (name, key)
             checked += len(digests)
+    for name, case in record.get("qk", {}).items():
+        inp = R.qk_inputs(case["tokens"], case["heads"], case["head_dim"], case["rotary_dim"], case["seed"], DEV)
+        got = K.qk_norm_rope(inp.q, inp.k, inp.norm_q, inp.norm_k, (inp.cos, inp.sin))
+        assert [R.digest(t) for t in got] == case["sha256"], name
+        checked += 2
     assert checked >= 30
+
+
+@pytest.mark.parametrize("s,h,d,rot", [(2048, 48, 128, 128), (1000, 16, 128, 64), (1025, 8, 96, 96),
+                                       (700, 8, 64, 32)])
+def test_qk_norm_rope_equals_the_compiled_reference(ref, s, h, d, rot):
+    """Q/K RMSNorm + RoPE on strided views of one fused QKV output, launched
+    for the reference the way its FusedAttention does (model/fusion.py:29-54;
+    on B200 without the ordered reduction, which it enables only on Hopper)."""
+    import triton
+    rk = ref.kernels
+    g = torch.Generator(device=DEV).manual_seed(s + d + rot)
+    qkv = torch.randn(1, s, 3 * h * d, device=DEV, generator=g).bfloat16()
+    q, k, _ = [t.unflatten(-1, (h, -1)) for t in qkv.chunk(3, dim=-1)]
+    nq = SimpleNamespace(weight=(1 + 0.05 * torch.randn(d, device=DEV, generator=g)).bfloat16(), eps=1e-6)
+    nk = SimpleNamespace(weight=(1 + 0.05 * torch.randn(d, device=DEV, generator=g)).bfloat16(), eps=1e-6)
+    phase = torch.randn(s, rot, device=DEV, generator=g)
+    cos, sin = phase.cos(), phase.sin()
+    q_out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    k_out = torch.empty_like(k, memory_format=torch.contiguous_format)
+    common = (q, k, nq.weight, nk.weight, cos, sin, q_out, k_out, s, h, q.stride(1), q.stride(2),
+              k.stride(1), k.stride(2), d)
+    grid = (q.numel() // d,)
+    if rot == d:
+        rk._qk_norm_full_rope_paired_kernel[grid](*common, float(nq.eps), triton.next_power_of_2(d // 2),
+                                                 num_warps=4, enable_fp_fusion=False)
+    else:
+        rk._qk_norm_rope_kernel[grid](*common, rot, float(nq.eps), triton.next_power_of_2(d), num_warps=4,
+                                      enable_fp_fusion=False)
+    oq, ok = K.qk_norm_rope(q, k, nq, nk, (cos, sin))
+    same(oq, q_out)
+    same(ok, k_out)

@@ -118,12 +118,13 @@ def test_tree_sum_is_a_sum():
         np.testing.assert_allclose(O.sumsq_tree(v), exact, rtol=2e-6)
 
 
-def test_chunk8_sum_is_a_sum():
+def test_qk_sums_are_sums():
     rng = np.random.default_rng(3)
     for width in (8, 64, 96, 128, 256):
         v = O.bf16_round(rng.standard_normal((5, width)).astype(np.float32))
         exact = np.sum(v.astype(np.float64) ** 2, axis=1)
-        np.testing.assert_allclose(O.sumsq_chunk8(v), exact, rtol=2e-6)
+        for rot in (width, width // 2):
+            np.testing.assert_allclose(O.sumsq_qk(v, rot), exact, rtol=2e-6)
 
 
 def test_bf16_rounding_matches_torch():
