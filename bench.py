@@ -47,11 +47,13 @@ def parse_args():
     p.add_argument("--cpu-sample-rows", type=int, default=512)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=["block", "stack", "sweep", "flash"], default="block",
+    p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels"], default="block",
                    help="block: config 2 per GPU (weak scaling); stack: config 4, 42 blocks x 3 denoiser "
                         "steps on 64512 tokens sharded over the GPUs with a final all-gather; sweep: "
                         "config 3 GEMM shapes, row-sharded, TOP/s per shape beside cuBLASLt; flash: one "
-                        "block at the released Flash shapes through the fused-block caller, attention included")
+                        "block at the released Flash shapes through the fused-block caller, attention included; "
+                        "reference_kernels: each kernel beside the reference's compiled GPU kernel (installed in "
+                        "baseline/_ref) on the same inputs, device time and output identity")
     p.add_argument("--layers", type=int, default=42)
     p.add_argument("--stack-tokens", type=int, default=64512)
     p.add_argument("--compress", action="store_true",
@@ -769,6 +771,115 @@ def run_flash(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_reference_kernels(args, rank, world, local):
+    """The path's kernels beside the reference's own compiled GPU kernels on
+    one B200 (the reference installed into baseline/_ref): per op, the device
+    time of each (CUDA-graph replay of `steps` calls, warm) and whether the
+    outputs are identical. The reference's INT8 GEMM kernel does not compile
+    under this image's Triton, so its int8_matmul runs its PyTorch path
+    (cuBLASLt integer GEMM + torch epilogue), which is what it executes here."""
+    if rank != 0:
+        return
+    import warnings
+    from types import SimpleNamespace
+    ref_root = Path(__file__).resolve().parent / "baseline" / "_ref"
+    if not (ref_root / "lynnreal" / "model" / "kernels.py").exists():
+        print(json.dumps({"workload": "reference_kernels", "unavailable": "reference not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, str(ref_root))
+    import triton
+    import lynnreal.model.int8_gemm as rg
+    import lynnreal.model.kernels as rk
+    from lynnreal_omni_b200 import _lib, kernels as K
+    from lynnreal_omni_b200.int8_gemm import int8_matmul
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _lib.load()
+    _lib.set_arithmetic("reference_gpu")
+    g = torch.Generator(device=dev).manual_seed(0)
+    m, d, inner = args.tokens, 6144, 14336
+
+    def device_us(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        graph.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        del graph
+        return t0.elapsed_time(t1) / reps * 1e3
+
+    x = torch.randn(1, m, d, device=dev, generator=g).bfloat16()
+    y = torch.randn(1, m, d, device=dev, generator=g).bfloat16()
+    norm = SimpleNamespace(weight=(1 + 0.05 * torch.randn(d, device=dev, generator=g)).bfloat16(), eps=1e-6)
+    table = (0.1 * torch.randn(1, 6 * d, device=dev, generator=g)).bfloat16()
+    idx = torch.zeros(m, dtype=torch.int64, device=dev)
+    xw = torch.randn(m, 4 * d, device=dev, generator=g).bfloat16()
+    proj = torch.randn(m, 2 * inner, device=dev, generator=g).bfloat16()
+    heads = 48
+    qkv = torch.randn(1, m, 3 * heads * 128, device=dev, generator=g).bfloat16()
+    q, k, _ = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+    phase = torch.randn(m, 128, device=dev, generator=g)
+    cos, sin = phase.cos(), phase.sin()
+
+    def ref_qk():
+        q_out = torch.empty_like(q, memory_format=torch.contiguous_format)
+        k_out = torch.empty_like(k, memory_format=torch.contiguous_format)
+        rk._qk_norm_full_rope_paired_kernel[(q.numel() // 128,)](
+            q, k, norm.weight[:128], norm.weight[128:256], cos, sin, q_out, k_out, m, heads, q.stride(1),
+            q.stride(2), k.stride(1), k.stride(2), 128, 1e-6, 64, num_warps=4, enable_fp_fusion=False)
+        return q_out, k_out
+
+    nq = SimpleNamespace(weight=norm.weight[:128], eps=1e-6)
+    nk = SimpleNamespace(weight=norm.weight[128:256], eps=1e-6)
+    ops = [
+        ("quantize_rows", [m, d], lambda: K.quantize_rows(x.view(m, d)), lambda: rk.quantize_rows(x.view(m, d))),
+        ("quantize_rows", [m, 4 * d], lambda: K.quantize_rows(xw), lambda: rk.quantize_rows(xw)),
+        ("_rms_adaln_quant_int8", [m, d], lambda: K._rms_adaln_quant_int8(x, norm, table, idx, 0, 1),
+         lambda: rk._rms_adaln_quant_int8(x, norm, table, idx, 0, 1)),
+        ("_rms_adaln", [m, d], lambda: K._rms_adaln(x, norm, table, idx, 3, 4),
+         lambda: rk._rms_adaln(x, norm, table, idx, 3, 4)),
+        ("residual_rms_quant", [m, d], lambda: K.residual_rms_quant(x, y, norm, table, idx),
+         lambda: rk.residual_rms_quant(x, y, norm, table, idx)),
+        ("_gated_residual", [m, d], lambda: K._gated_residual(x, y, table, idx, 2),
+         lambda: rk._gated_residual(x, y, table, idx, 2)),
+        ("_swiglu", [m, 2 * inner], lambda: K._swiglu(proj), lambda: rk._swiglu(proj)),
+        ("_swiglu_quant_int8", [m, 2 * inner], lambda: K._swiglu_quant_int8(proj), lambda: rk._swiglu_quant_int8(proj)),
+        ("qk_norm_rope (full rotary)", [m, heads, 128], lambda: K.qk_norm_rope(q, k, nq, nk, (cos, sin)), ref_qk),
+    ]
+    for kk, nn in ((d, d), (d, 4 * d), (4 * d, d)):
+        a = torch.randint(-127, 128, (m, kk), generator=g, device=dev, dtype=torch.int8)
+        b = torch.randint(-127, 128, (nn, kk), generator=g, device=dev, dtype=torch.int8).t()
+        rs = torch.rand(m, 1, generator=g, device=dev) / 127
+        cs = torch.rand(1, nn, generator=g, device=dev) / 127
+        bias = (0.02 * torch.randn(nn, generator=g, device=dev)).bfloat16()
+        ops.append(("int8_matmul", [m, kk, nn], (lambda a=a, b=b, rs=rs, cs=cs, bias=bias: int8_matmul(a, b, rs, cs, bias)),
+                    (lambda a=a, b=b, rs=rs, cs=cs, bias=bias: rg.int8_matmul(a, b, rs, cs, bias))))
+    rows = []
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")  # the reference reports its GEMM falling back to its torch path
+        for name, shape, ours, theirs in ops:
+            a_out, b_out = ours(), theirs()
+            a_out = a_out if isinstance(a_out, tuple) else (a_out,)
+            b_out = b_out if isinstance(b_out, tuple) else (b_out,)
+            identical = all(torch.equal(u, v) for u, v in zip(a_out, b_out))
+            reps = max(3, args.steps)
+            t_ours, t_ref = device_us(ours, reps), device_us(theirs, reps)
+            rows.append({"op": name, "shape": shape, "ours_us": round(t_ours, 1), "reference_us": round(t_ref, 1),
+                         "speedup": round(t_ref / t_ours, 2), "identical": identical})
+    print(json.dumps({"workload": "reference_kernels", "gpu": torch.cuda.get_device_name(dev),
+                      "arithmetic": _lib.arithmetic(), "timing": "CUDA-graph replay, device time per call",
+                      "reference": f"baseline/_ref, Triton {triton.__version__}", "ops": rows}))
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
@@ -782,6 +893,8 @@ def main():
         run_sweep(args, rank, world, local)
     elif args.workload == "flash":
         run_flash(args, rank, world, local)
+    elif args.workload == "reference_kernels":
+        run_reference_kernels(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

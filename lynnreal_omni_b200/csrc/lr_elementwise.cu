@@ -610,45 +610,35 @@ __global__ void __launch_bounds__(kThreads, LR_SWIGLU_MINB) swiglu_kernel(const 
 // touches (256 is a multiple of L), so its weights and cos/sin are loaded once
 // per token; the rotary partner chunk is lane p ^ (rotary_dim / 16) of the
 // same head. All NI chunk loads of a thread are issued before any compute.
-// A reduction as a layout of threads holding S consecutive terms each runs it:
-// each thread adds its terms in order, then xor butterflies over the
-// 32-thread warps and over the warps. `t` are this lane's 8 consecutive terms;
-// the head's terms span `lanes` lanes (a power of two).
-template <int S>
-__device__ __forceinline__ float spt_sum(const float (&t)[8], int lanes) {
-  constexpr int J = 8 / S;  // emulated threads per lane
-  float v[J];
+// The sum that threads holding one term each compute with xor butterflies over
+// their 32-thread warps and then over the warps, as seen from thread 0 (the
+// butterfly leaves that value in every thread): at offset o, thread T adds
+// thread T + o. Here lane p holds the terms T = 8p .. 8p+7 in v; the terms
+// span n_lanes lanes (a power of two) from this lane group's first lane, which
+// returns the total. Offsets 16 and 8 are lanes 2 and 1 away, 4, 2 and 1 are
+// inside a lane, and warp w's sum sits in lane 4w.
+__device__ __forceinline__ float thread_tree_sum(float (&v)[8], int n_lanes) {
+  const int n = n_lanes * 8;
+  if (n >= 32) {
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    float acc = t[j * S];
-#pragma unroll
-    for (int e = 1; e < S; ++e) acc = __fadd_rn(acc, t[j * S + e]);
-    v[j] = acc;
+    for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_down_sync(0xffffffffu, v[j], 2));
   }
-  const int n = lanes * J;
-  const int wt = n < 32 ? n : 32;
-  for (int off = wt >> 1; off > 0; off >>= 1) {
-    if (off >= J) {
+  if (n >= 16) {
 #pragma unroll
-      for (int j = 0; j < J; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], off / J));
-    } else {
-      float w[J];
-#pragma unroll
-      for (int j = 0; j < J; ++j) w[j] = __fadd_rn(v[j], v[j ^ off]);
-#pragma unroll
-      for (int j = 0; j < J; ++j) v[j] = w[j];
-    }
+    for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_down_sync(0xffffffffu, v[j], 1));
   }
-  for (int off = (n / 32) >> 1; off > 0; off >>= 1) {
 #pragma unroll
-    for (int j = 0; j < J; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], off * 32 / J));
-  }
+  for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(v[j], v[j + 4]);
+  v[0] = __fadd_rn(v[0], v[2]);
+  v[1] = __fadd_rn(v[1], v[3]);
+  v[0] = __fadd_rn(v[0], v[1]);
+  for (int ow = (n >> 5) >> 1; ow > 0; ow >>= 1) v[0] = __fadd_rn(v[0], __shfl_down_sync(0xffffffffu, v[0], 4 * ow));
   return v[0];
 }
 
 // Head-row sum of squares of the Q/K kernels in the order of the reference's
 // compiled Q/K kernels (4 warps, one term per thread, so exact for head
-// dimensions up to 128). `f` are this lane's 8 values (columns 8p .. 8p+7 of
+// dimensions up to 128; thread_tree_sum). `f` are this lane's 8 values (columns 8p .. 8p+7 of
 // the head row), `raw` the same as packed bf16; the head's lanes start at
 // `base`.
 //   * full rotary (paired): terms x_i^2 + x_{i+D/2}^2 for i < D/2
@@ -675,7 +665,7 @@ __device__ __forceinline__ float qk_sumsq(const float (&f)[8], const uint4& raw,
 #pragma unroll
     for (int e = 0; e < 8; ++e) t[e] = __fmul_rn(f[e], f[e]);
   }
-  const float total = spt_sum<1>(t, n_lanes);
+  const float total = thread_tree_sum(t, n_lanes);
   return __shfl_sync(0xffffffffu, total, base);
 }
 
