@@ -14,12 +14,13 @@
 #include "lr_common.cuh"
 #include "lr_host.h"
 
-// Minimum resident CTAs per SM requested for the persistent RMSNorm kernel on
-// rows of up to 4 chunks per thread (a register cap: 4 -> 64 registers, 32
-// warps per SM; measured 5 % faster than the compiler's 80 registers, 3 CTAs
-// per SM). Wider rows keep the compiler's allocation. Tuning knob.
+// Minimum resident CTAs per SM requested for the one-row RMSNorm kernel on
+// rows of up to 4 chunks per thread (a register cap when nonzero). With the
+// reference's summation order the compiler's own allocation is faster
+// (12240 x 6144: K4 81.2 -> 78.4 us, K3 58.5 -> 56.4 us against a cap of 4, 64
+// registers). Tuning knob.
 #ifndef LR_RMS_MINB
-#define LR_RMS_MINB 4
+#define LR_RMS_MINB 0
 #endif
 // The same caps for the two-row residual RMSNorm kernel on rows of up to 3
 // chunks per thread (K8: 3 -> 80 registers, 3 CTAs per SM; 123 -> 108 us at
@@ -988,6 +989,15 @@ bool vec_ok(int64_t hidden, std::initializer_list<const void*> ptrs) {
 
 }  // namespace
 
+// The gated residual (K5) and the bf16-output RMSNorm (K3) run one row per CTA
+// (grid = rows) instead of the persistent prefetching grid: 70.8 -> 66.8 us
+// and 60.0 -> 58.5 us at 12240 x 6144. Tuning knobs.
+#ifndef LR_K5_ONE
+#define LR_K5_ONE 1
+#endif
+#ifndef LR_K3_ONE
+#define LR_K3_ONE 1
+#endif
 #ifndef LR_RMS2_OFF
 #define LR_RMS2_OFF 0  // 1: the residual variant runs the one-row kernel too (tuning knob)
 #endif
@@ -1003,7 +1013,7 @@ static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, 
   if (R && kC <= 4 && !LR_RMS2_OFF)                                                               \
     lr::rms_mod2_kernel<(kC <= 4 ? kC : 4), V, R, M, Q><<<(unsigned)((rows + 1) / 2), lr::kThreads, 0, s>>>(a); \
   else                                                                                            \
-    lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(a)
+    lr::rms_mod_kernel<kC, V, R, M, Q><<<lr::persistent_grid(lr::rms_mod_kernel<kC, V, R, M, Q>, rows, lr::Prefetch<kC>::kOn && !(LR_K3_ONE && !Q)), lr::kThreads, 0, s>>>(a)
 #define LR_RMS_Q(V, R, M)  \
   if (quant) { LR_RMS(V, R, M, true); } else { LR_RMS(V, R, M, false); }
 #define LR_RMS_M(V, R)     \
@@ -1108,10 +1118,10 @@ extern "C" int lr_gated_residual(const void* x, const void* y, const void* table
   bf16* op = static_cast<bf16*>(out);
   LR_CHUNK_DISPATCH(C, {
     if (vec)
-      lr::gated_residual_kernel<kC, true><<<lr::persistent_grid(lr::gated_residual_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(
+      lr::gated_residual_kernel<kC, true><<<lr::persistent_grid(lr::gated_residual_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn && !LR_K5_ONE), lr::kThreads, 0, s>>>(
           xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op, rows);
     else
-      lr::gated_residual_kernel<kC, false><<<lr::persistent_grid(lr::gated_residual_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(
+      lr::gated_residual_kernel<kC, false><<<lr::persistent_grid(lr::gated_residual_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn && !LR_K5_ONE), lr::kThreads, 0, s>>>(
           xp, yp, tp, table_rows, table_width, indices, sequence, (int)hidden, gate_slot, op, rows);
   });
   return lr::launch_status("gated_residual");
