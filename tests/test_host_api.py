@@ -158,3 +158,14 @@ def test_c_header_compiles_as_c():
         r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-I", str(ROOT / "include"),
                             str(c)], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_arithmetic_mode_rejects_unknown_modes_without_a_gpu():
+    """lr_set_arithmetic validates its argument on the host, before any CUDA
+    call; the Python wrapper refuses names it does not know."""
+    lib = _lib.load()
+    assert lib.lr_set_arithmetic(7) == _lib.LR_ERR_INVALID_ARGUMENT
+    assert b"unknown mode" in lib.lr_last_error()
+    assert lib.lr_get_arithmetic(None) == _lib.LR_ERR_INVALID_ARGUMENT
+    with pytest.raises(ValueError):
+        _lib.set_arithmetic("fast")
