@@ -100,6 +100,17 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return __fdividef(x, __fadd_rn(1.0f, __expf(-two_u)));
 }
 
+// The same for two values with packed fp32 arithmetic (each lane rounds
+// exactly as the scalar form does, so the results are identical).
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+  const float2 beta2 = make_float2(1.5957691216057308f, 1.5957691216057308f);
+  const float2 kappa = make_float2(0.044715f, 0.044715f);
+  const float2 x3 = __fmul2_rn(__fmul2_rn(x, x), x);
+  const float2 two_u = __fmul2_rn(beta2, __fadd2_rn(x, __fmul2_rn(kappa, x3)));
+  const float2 den = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(__expf(-two_u.x), __expf(-two_u.y)));
+  return make_float2(__fdividef(x.x, den.x), __fdividef(x.y, den.y));
+}
+
 // Final bf16 value of one output element. `d` already holds the dequantised
 // fp32 value including bias; `resid`/`gate` are used by kGated only.
 template <int EPI>
@@ -354,13 +365,22 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
   static_assert(W % 8 == 0, "chunk width");
   const float4* cs4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
   float d[W];
+  const float2 rs2 = make_float2(rs, rs);
 #pragma unroll
   for (int q = 0; q < W / 4; ++q) {
+    // (float(acc) * row_scale) * col_scale, two columns per packed multiply
+    // (each lane rounds as dequant() does)
     const float4 c = __ldg(cs4 + q);
-    d[4 * q + 0] = dequant((int32_t)acc[4 * q + 0], rs, c.x);
-    d[4 * q + 1] = dequant((int32_t)acc[4 * q + 1], rs, c.y);
-    d[4 * q + 2] = dequant((int32_t)acc[4 * q + 2], rs, c.z);
-    d[4 * q + 3] = dequant((int32_t)acc[4 * q + 3], rs, c.w);
+    const float2 lo = __fmul2_rn(__fmul2_rn(make_float2(__int2float_rn((int32_t)acc[4 * q + 0]),
+                                                        __int2float_rn((int32_t)acc[4 * q + 1])), rs2),
+                                 make_float2(c.x, c.y));
+    const float2 hi = __fmul2_rn(__fmul2_rn(make_float2(__int2float_rn((int32_t)acc[4 * q + 2]),
+                                                        __int2float_rn((int32_t)acc[4 * q + 3])), rs2),
+                                 make_float2(c.z, c.w));
+    d[4 * q + 0] = lo.x;
+    d[4 * q + 1] = lo.y;
+    d[4 * q + 2] = hi.x;
+    d[4 * q + 3] = hi.y;
   }
   if (ep.bias != nullptr) {
     const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + col0);
@@ -369,7 +389,11 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
       float b[8];
       unpack8(__ldg(b4 + q), b);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) d[8 * q + e] = __fadd_rn(d[8 * q + e], b[e]);
+      for (int e = 0; e < 8; e += 2) {
+        const float2 s2 = __fadd2_rn(make_float2(d[8 * q + e], d[8 * q + e + 1]), make_float2(b[e], b[e + 1]));
+        d[8 * q + e] = s2.x;
+        d[8 * q + e + 1] = s2.y;
+      }
     }
   }
   uint4* dst = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col0);
@@ -382,7 +406,11 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
     if (EPI == kGelu) {
       unpack8(y, o);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = gelu_tanh(o[e]);
+      for (int e = 0; e < 8; e += 2) {
+        const float2 g2 = gelu_tanh2(make_float2(o[e], o[e + 1]));
+        o[e] = g2.x;
+        o[e + 1] = g2.y;
+      }
       y = pack8(o);
     } else if (EPI == kGated) {
       // bf16(x + bf16(gate * bf16(dequant)))   (model/kernels.py:146-153)
