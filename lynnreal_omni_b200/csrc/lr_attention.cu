@@ -111,13 +111,26 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
     }
   }
 }
-// Warp-wide bounded wait: lane 0 polls, the warp reconverges before any
-// .sync.aligned tensor-memory instruction that follows.
+// Warp-wide bounded wait: every lane polls the barrier and the warp moves on
+// together once any lane has seen the phase complete (phases only move
+// forward), so no lane waits in a divergent branch.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int lane) {
-  int ok = 1;
-  if (lane == 0) ok = wait_bounded(bar, parity, abort_flag) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  return ok != 0;
+  if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    int stop = 0;
+    if (lane == 0) {
+      if (*abort_flag) {
+        stop = 1;
+      } else if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1u;
+        atomicOr(&g_attn_status, (unsigned)kDevErrWaitTimeout);
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+  }
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x,
                                             int32_t y, int32_t z) {
