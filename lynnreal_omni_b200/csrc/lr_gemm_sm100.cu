@@ -361,7 +361,8 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
 template <int EPI, int W = 32>
 __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[W],
                                                 int64_t row, int col0, float rs,
-                                                const bf16* gate_ptr, bool have_gate) {
+                                                const bf16* gate_ptr, bool have_gate,
+                                                const uint4* resid_pre = nullptr) {
   static_assert(W % 8 == 0, "chunk width");
   const float4* cs4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
   float d[W];
@@ -414,7 +415,8 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
       y = pack8(o);
     } else if (EPI == kGated) {
       // bf16(x + bf16(gate * bf16(dequant)))   (model/kernels.py:146-153)
-      const uint4 x = *reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col0 + 8 * q);
+      const uint4 x = resid_pre != nullptr ? resid_pre[q]
+                                            : *reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col0 + 8 * q);
       const uint32_t gd = (ep.table == nullptr) ? kBf2One : 0u;
       const uint4 g = have_gate ? __ldg(reinterpret_cast<const uint4*>(gate_ptr + col0 + 8 * q))
                                 : make_uint4(gd, gd, gd, gd);
@@ -479,8 +481,21 @@ __device__ __forceinline__ void drain_accumulator(const EpiArgs& ep, int M, int 
       }
     }
   }
+  // Gated residual: each chunk's residual row segment is loaded one chunk
+  // ahead, so its memory latency overlaps the previous chunk's epilogue.
+  uint4 xr[4] = {}, xn[4] = {};
+  auto load_resid = [&](int c, uint4 (&dst)[4]) {
+    const int col = col_base + c * 32;
+    if (row_ok && col + 32 <= N) {
+      const uint4* src = reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = src[q];
+    }
+  };
+  if (EPI == kGated) load_resid(0, xr);
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
+    if (EPI == kGated && c + 1 < BN / 32) load_resid(c + 1, xn);
     uint32_t r[32];
     tmem_ld32(tbase + (uint32_t)(c * 32), r);
     if (c == BN / 32 - 1) {
@@ -506,9 +521,13 @@ __device__ __forceinline__ void drain_accumulator(const EpiArgs& ep, int M, int 
         store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
       }
     } else if (col0 + 32 <= N) {
-      store_chunk_vec<EPI>(ep, r, row, col0, rs, gptr, have_gate);
+      store_chunk_vec<EPI>(ep, r, row, col0, rs, gptr, have_gate, EPI == kGated ? xr : nullptr);
     } else {
       store_chunk_tail<EPI>(ep, r, row, col0, N, rs, gptr, have_gate);
+    }
+    if (EPI == kGated) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xr[q] = xn[q];
     }
   }
 }
