@@ -19,7 +19,7 @@
 //              query row (= TMEM lane) and one 64-key half of every score
 //              tile; the halves exchange row maxima (and, at the end, sums)
 //              through shared memory with bounded mbarrier waits. Running max
-//              and sum in fp32 with exp2 (a quarter of each full tile's
+//              and sum in fp32 with exp2 (a sixteenth of each full tile's
 //              exponentials on the FMA pipe); the max moves only when it grows
 //              by more than 2^8 (exact, since O and l share it), so O is
 //              rescaled in TMEM rarely, after its previous P V has finished;
@@ -40,7 +40,7 @@
 // Exponentials evaluated on the FMA pipe instead of the MUFU unit: every
 // LR_ATTN_EMU-th pair of a full key tile (0: none). Tuning knob.
 #ifndef LR_ATTN_EMU
-#define LR_ATTN_EMU 4
+#define LR_ATTN_EMU 16
 #endif
 
 namespace lr {
