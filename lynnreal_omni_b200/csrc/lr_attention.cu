@@ -17,15 +17,19 @@
 //              TMEM (A operand), V as an MN-major operand from its TMA tile;
 //   warps 2-9  softmax: two warps per TMEM lane quadrant, each thread owning a
 //              query row (= TMEM lane) and one 64-key half of every score
-//              tile; the halves exchange row maxima (and, at the end, sums)
-//              through shared memory with bounded mbarrier waits. Running max
-//              and sum in fp32 with exp2 (a sixteenth of each full tile's
-//              exponentials on the FMA pipe); the max moves only when it grows
-//              by more than 2^8 (exact, since O and l share it), so O is
-//              rescaled in TMEM rarely, after its previous P V has finished;
-//              P(j) is written as bf16 pairs over consumed score columns; at
-//              the end O / l -> bf16 -> global.
-// TMEM columns: score buffers at 0 and 128, O at 256 (512 allocated).
+//              tile. Each half keeps its own running max and sum (fp32, exp2,
+//              a sixteenth of each full tile's exponentials on the FMA pipe)
+//              and its own O accumulator, so the halves never wait for each
+//              other within the key loop; the max moves only when it grows by
+//              more than 2^8 (exact, since O and l share it), so O is rescaled
+//              in TMEM rarely, after its previous P V has finished. P(j) of a
+//              half is written as bf16 pairs over the first 32 of its own score
+//              columns. At the end the halves exchange max and sum once through
+//              shared memory (bounded mbarrier wait) and each warp writes 64
+//              output columns: (O_a 2^(m_a-M) + O_b 2^(m_b-M)) / (l_a 2^(m_a-M)
+//              + l_b 2^(m_b-M)) -> bf16 -> global.
+// TMEM columns: score buffers at 0 and 128, O_a (keys [0, 64) of every tile)
+// at 256, O_b (keys [64, 128)) at 384; 512 allocated.
 // Every mbarrier wait is bounded (2 s): on timeout the kernel raises a status
 // bit, lets its own copies and MMAs finish, frees TMEM and returns.
 // No TMA multicast.
@@ -61,12 +65,12 @@ constexpr int NUM_THREADS = 64 + 32 * SOFTMAX_WARPS;
 constexpr int SMEM_Q = 0;
 constexpr int SMEM_K = TILE;                        // K slots
 constexpr int SMEM_V = SMEM_K + K_SLOTS * TILE;     // V slots
-constexpr int SMEM_RED = SMEM_V + V_SLOTS * TILE;   // [parity][half][row] fp32
+constexpr int SMEM_RED = SMEM_V + V_SLOTS * TILE;   // [max | sum][half][row] fp32
 constexpr int SMEM_BAR = SMEM_RED + 2 * 2 * BQ * 4;
 constexpr int BAR_BYTES = 512;
 constexpr size_t SMEM_BYTES = 1024 + SMEM_BAR + BAR_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_O = 256;  // score buffers at 0 and 128, O at 256
+constexpr uint32_t COL_O = 256;  // score buffers at 0 and 128, O_a at 256, O_b at 384
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // ------------------------------------------------------------- PTX wrappers
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* pv_done = bars + 15;     // P(j) V_j done (commit, every j)
   uint64_t* o_done = bars + 16;      // last P V done (commit)
   uint64_t* drain = bars + 17;       // MMA drain before TMEM is freed
-  uint64_t* xbar = bars + 18;        // [quadrant][parity] row exchange between a row's two halves (2 warps)
+  uint64_t* xbar = bars + 18;        // [quadrant] final max / sum exchange of a row's two halves (2 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
   static_assert(26 * 8 + 8 <= BAR_BYTES, "barrier region");
   volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -342,7 +346,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(smem_u32(pv_done), 1);
     mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(drain), 1);
-    for (int b = 0; b < 8; ++b) mbar_init(smem_u32(&xbar[b]), 2);
+    for (int b = 0; b < 4; ++b) mbar_init(smem_u32(&xbar[b]), 2);
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&map_q);
@@ -445,10 +449,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         // O += P(j) V_j, P(j) read from tensor memory (its score buffer).
         const uint32_t va = smem_u32(smem + SMEM_V + (j % V_SLOTS) * TILE);
+        // keys [0, 64) into O_a (P over score columns [0, 32)), keys [64, 128)
+        // into O_b (P over score columns [64, 96))
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_f16_ts(tmem + COL_O, tmem + (uint32_t)((j & 1) * BKV + kk * 8),
-                     desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV, (j | kk) != 0 ? 1u : 0u);
+          mma_f16_ts(tmem + COL_O + (kk >= 4 ? 128u : 0u), tmem + (uint32_t)((j & 1) * BKV + kk * 8 + (kk >= 4 ? 32 : 0)),
+                     desc_mnmajor(va + (uint32_t)(kk * 16 * 128)), kIdescPV, (j | (kk & 3)) != 0 ? 1u : 0u);
         mma_commit(smem_u32(pv_done));
         mma_commit(smem_u32(&v_empty[j % V_SLOTS]));
         if (j == tiles - 1) mma_commit(smem_u32(o_done));
@@ -463,17 +469,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // -------------------------------------------------------- softmax warps
     const int quad = warp & 3;          // TMEM lanes [32 quad, 32 quad + 32)
-    const int half = (warp - 2) >> 2;   // keys / output columns [64 half, 64 half + 64)
+    const int half = (warp - 2) >> 2;   // keys [64 half, 64 half + 64) of every tile
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t o_col = tmem + lane_off + COL_O + (uint32_t)(half * 64);
-    float* red = reinterpret_cast<float*>(smem + SMEM_RED);  // [parity][half][row]
-    uint64_t* xq = xbar + quad * 2;                          // [parity]
+    const uint32_t o_own = tmem + lane_off + COL_O + (uint32_t)(half * 128);  // this half's O
+    float* red = reinterpret_cast<float*>(smem + SMEM_RED);  // [max | sum][half][row]
+    uint64_t* xq = xbar + quad;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < tiles; ++j) {
       const int par = j & 1;
-      const uint32_t s_col = tmem + lane_off + (uint32_t)(par * BKV);
+      const uint32_t s_col = tmem + lane_off + (uint32_t)(par * BKV + half * 64);
       // S(j) ready; the same commit covers P(j-2) V_{j-2} (issued before).
       if (!warp_wait(smem_u32(&s_full[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
         ok = false;
@@ -483,8 +489,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float s[64];
       {
         uint32_t ra[32], rb[32];
-        tmem_ld32_nowait(s_col + (uint32_t)(half * 64), ra);
-        tmem_ld32_nowait(s_col + (uint32_t)(half * 64 + 32), rb);
+        tmem_ld32_nowait(s_col, ra);
+        tmem_ld32_nowait(s_col + 32u, rb);
         tmem_wait_ld64(ra, rb);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -506,25 +512,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mx2 = fmaxf(mx2, s[e + 2]);
         mx3 = fmaxf(mx3, s[e + 3]);
       }
-      // Row max over both halves. Both halves have loaded their scores before
-      // either passes this exchange, so P (which overwrites score columns of
-      // the other half) is only written afterwards. A slot is rewritten two
-      // tiles later, after the partner has read it.
-      red[(par * 2 + half) * BQ + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&xq[par]));
-      if (!warp_wait(smem_u32(&xq[par]), (uint32_t)(j >> 1) & 1u, abort_flag, lane)) {
-        ok = false;
-        break;
-      }
-      const float tile_max = fmaxf(red[(par * 2) * BQ + row], red[(par * 2 + 1) * BQ + row]) * sh.scale_log2;
-      // Move the reference max only when it grows by more than 2^8 (both
-      // halves decide identically): p <= 256, O rescaled rarely, exact.
+      // This half's running max moves only when it grows by more than 2^8:
+      // p <= 256, O rescaled rarely, exact.
+      const float tile_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sh.scale_log2;
       const bool move = tile_max > m_run + 8.0f;
       const float m_use = move ? tile_max : m_run;
-      const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on the first tile
+      const float alpha = move ? ex2(m_run - m_use) : 1.0f;  // 0 on this half's first valid tile
+      const float m_sub = m_use == -INFINITY ? 0.0f : m_use;  // no valid key yet: p = 0
       const float2 sc2 = make_float2(sh.scale_log2, sh.scale_log2);
-      const float2 nm2 = make_float2(-m_use, -m_use);
+      const float2 nm2 = make_float2(-m_sub, -m_sub);
       float2 lsum = make_float2(0.0f, 0.0f);
       {
         uint32_t pk[32];
@@ -532,7 +528,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           softmax_half<LR_ATTN_EMU>(s, sc2, nm2, lsum, pk);
         else  // masked keys need an exact 0: MUFU only
           softmax_half<0>(s, sc2, nm2, lsum, pk);
-        tmem_st32(s_col + (uint32_t)(half * 32), pk);  // P(j) keys [64 half, +64) as bf16 pairs
+        tmem_st32(s_col, pk);  // P(j) of this half over its own first 32 score columns
       }
       l_run = fmaf(l_run, alpha, lsum.x + lsum.y);
       m_run = m_use;
@@ -543,58 +539,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        uint32_t oa[32], ob[32];
-        tmem_ld32_nowait(o_col, oa);
-        tmem_ld32_nowait(o_col + 32u, ob);
-        tmem_wait_ld64(oa, ob);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          oa[e] = __float_as_uint(__uint_as_float(oa[e]) * alpha);
-          ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
+        for (int c = 0; c < 128; c += 64) {
+          uint32_t oa[32], ob[32];
+          tmem_ld32_nowait(o_own + (uint32_t)c, oa);
+          tmem_ld32_nowait(o_own + (uint32_t)c + 32u, ob);
+          tmem_wait_ld64(oa, ob);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            oa[e] = __float_as_uint(__uint_as_float(oa[e]) * alpha);
+            ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
+          }
+          tmem_st32(o_own + (uint32_t)c, oa);
+          tmem_st32(o_own + (uint32_t)c + 32u, ob);
         }
-        tmem_st32(o_col, oa);
-        tmem_st32(o_col + 32u, ob);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&p_full[par]));
     }
-    // Each half holds the row sum over its keys against the same max; the
-    // exchange uses the parity the last tile did not (read by both already).
-    float l_other = 0.0f;
+    // The halves exchange their running max and sum once; each warp then
+    // writes output columns [64 half, +64) from both accumulators:
+    // O = (O_a 2^(m_a - M) + O_b 2^(m_b - M)) / (l_a 2^(m_a - M) + l_b 2^(m_b - M)).
+    float m_o = -INFINITY, l_o = 0.0f;
     if (ok) {
-      const int pe = tiles & 1;
-      red[(pe * 2 + half) * BQ + row] = l_run;
+      red[half * BQ + row] = m_run;
+      red[(2 + half) * BQ + row] = l_run;
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&xq[pe]));
-      ok = warp_wait(smem_u32(&xq[pe]), (uint32_t)(tiles >> 1) & 1u, abort_flag, lane);
-      if (ok) l_other = red[(pe * 2 + 1 - half) * BQ + row];
+      if (lane == 0) mbar_arrive(smem_u32(xq));
+      ok = warp_wait(smem_u32(xq), 0u, abort_flag, lane);
+      if (ok) {
+        m_o = red[(1 - half) * BQ + row];
+        l_o = red[(3 - half) * BQ + row];
+      }
     }
     if (ok && warp_wait(smem_u32(o_done), 0u, abort_flag, lane)) {
       tc_fence_after();
-      const float inv_l = 1.0f / (half == 0 ? l_run + l_other : l_other + l_run);
+      const float m_a = half == 0 ? m_run : m_o, m_b = half == 0 ? m_o : m_run;
+      const float l_a = half == 0 ? l_run : l_o, l_b = half == 0 ? l_o : l_run;
+      const float m_all = fmaxf(m_a, m_b);  // finite: key 0 is valid and in half 0
+      const float f_a = ex2(m_a - m_all), f_b = ex2(m_b - m_all);
+      const float inv_l = 1.0f / fmaf(l_a, f_a, l_b * f_b);
+      const float g_a = f_a * inv_l, g_b = f_b * inv_l;
       const int qrow = q0 + row;
-      uint32_t oa[32], ob[32];
-      tmem_ld32_nowait(o_col, oa);
-      tmem_ld32_nowait(o_col + 32u, ob);
-      tmem_wait_ld64(oa, ob);
-      if (qrow < sh.seq_q) {
-        uint4* d4 = reinterpret_cast<uint4*>(out + ((int64_t)batch * sh.seq_q + qrow) * sh.out_ts +
-                                             (int64_t)head * D + half * 64);
+      const uint32_t oa_col = tmem + lane_off + COL_O + (uint32_t)(half * 64);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float f[8];
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t oa[32], ob[32];
+        tmem_ld32_nowait(oa_col + (uint32_t)c, oa);
+        tmem_ld32_nowait(oa_col + 128u + (uint32_t)c, ob);
+        tmem_wait_ld64(oa, ob);
+        if (qrow < sh.seq_q) {
+          uint4* d4 = reinterpret_cast<uint4*>(out + ((int64_t)batch * sh.seq_q + qrow) * sh.out_ts +
+                                               (int64_t)head * D + half * 64 + c);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(oa[8 * q + e]) * inv_l;
-          d4[q] = pack8(f);
-        }
+          for (int q = 0; q < 4; ++q) {
+            float f[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(ob[8 * q + e]) * inv_l;
-          d4[4 + q] = pack8(f);
+            for (int e = 0; e < 8; ++e)
+              f[e] = fmaf(__uint_as_float(oa[8 * q + e]), g_a, __uint_as_float(ob[8 * q + e]) * g_b);
+            d4[q] = pack8(f);
+          }
         }
       }
     }

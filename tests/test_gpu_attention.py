@@ -42,6 +42,9 @@ def check_close(got, ref, q, k, v, scale):
     (2, 300, 300, 3, 1.0),     # ragged query and key tiles
     (1, 1000, 1000, 2, 1.0),
     (1, 200, 77, 4, 1.0),      # cross attention, one partial key tile
+    (1, 96, 50, 2, 1.0),       # fewer than 64 keys: the second key half of every row is empty
+    (1, 130, 64, 1, 4.0),      # exactly one key half
+    (1, 257, 65, 2, 8.0),      # the second key half holds one key
     (1, 4096, 4096, 2, 1.0),   # long rows: 32 key tiles
     (2, 513, 640, 2, 4.0),     # peaked scores: the running max moves often
 ])
