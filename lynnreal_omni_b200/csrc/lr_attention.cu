@@ -284,7 +284,7 @@ __device__ __forceinline__ void softmax_half(const float* s, float2 sc2, float2 
   for (int q = 0; q < 32; ++q) {
     const float2 x = __ffma2_rn(make_float2(s[2 * q], s[2 * q + 1]), sc2, nm2);
     float2 p;
-    if (EMU > 0 && (q % EMU) == EMU - 1)
+    if (EMU > 0 && (q % (EMU > 0 ? EMU : 1)) == EMU - 1)
       p = exp2_poly2(x);
     else
       p = make_float2(ex2(x.x), ex2(x.y));
