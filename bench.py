@@ -6,13 +6,17 @@
 For N > 1 launch one process per GPU with torch.distributed.run. A step is one
 forward of the W8A8 path of one Flash-like DiT block (config 2: M=12240 tokens,
 D=6144, QKV 18432, FFN 24576 GELU-tanh, cross-attention Q/O with text K/V from a
-512x4096 context) on each GPU's own 12240-token latent; weights are replicated
-and no data crosses GPUs (weak scaling: the path is independent per token row).
-The timed region holds exactly K steps between a barrier and a device
-synchronize; the step time is the maximum over ranks of CUDA-event time.
+512x4096 context) over one 12240-token latent whose token rows are split into
+contiguous blocks, one per GPU (1530 rows each at N=8), with the int8 weights
+replicated; every step ends with one NCCL all_gather_into_tensor of the bf16
+block output, inside the timed region (strong scaling: the path is independent
+per token row, the gather is its only exchange). The timed region holds exactly
+K steps between a barrier and a device synchronize; the step time is the
+maximum over ranks of CUDA-event time.
 
 ``--impl reference`` times the reference's own PyTorch CPU implementation of
-the same path (the torch port under oracle/) on the host cores, rank 0 only.
+the same block (the torch port under oracle/) on the host cores, rank 0 only,
+all 12240 rows every step.
 """
 from __future__ import annotations
 
@@ -43,8 +47,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--tokens", type=int, default=12240, help="token rows per GPU")
-    p.add_argument("--cpu-sample-rows", type=int, default=512)
+    p.add_argument("--tokens", type=int, default=12240,
+                   help="block: token rows of the latent, sharded over the GPUs; flash: token rows per GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels"], default="block",
@@ -69,44 +73,61 @@ def dist_env():
     return rank, world, local
 
 
-def bind_local_numa(local_rank: int):
+def bind_local_numa(local_rank: int) -> dict:
     """Run this rank on the CPUs local to its GPU's PCIe root (sysfs), so its
-    pinned host buffers are first touched on that NUMA node. Best effort:
-    returns the node, or None when the topology is not visible."""
+    pinned host buffers are first touched next to the GPU. Best effort: the
+    result records the NUMA node, the CPUs bound and, when nothing was bound,
+    why (a node of -1 means the platform reports no NUMA locality)."""
+    info = {"node": None, "cpus": None, "reason": None}
     try:
         props = torch.cuda.get_device_properties(local_rank)
         dev = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
         base = Path("/sys/bus/pci/devices") / dev
+        info["pci"] = dev
         node = int((base / "numa_node").read_text().strip())
+        info["node"] = node
         cpus = set()
         for part in (base / "local_cpulist").read_text().strip().split(","):
             lo, _, hi = part.partition("-")
             cpus.update(range(int(lo), int(hi or lo) + 1))
-        cpus &= os.sched_getaffinity(0) or cpus
-        if node < 0 or not cpus:
-            return None
-        os.sched_setaffinity(0, cpus)
-        return node
-    except (OSError, ValueError, AttributeError):
-        return None
+        allowed = os.sched_getaffinity(0)
+        local = cpus & allowed
+        if not local:
+            info["reason"] = "no CPU of local_cpulist is in this process's affinity"
+            return info
+        if local == allowed:
+            info["reason"] = "every allowed CPU is already local to the GPU (nothing to bind)"
+            info["cpus"] = len(local)
+            return info
+        os.sched_setaffinity(0, local)
+        info["cpus"] = len(local)
+        return info
+    except (OSError, ValueError, AttributeError) as error:
+        info["reason"] = f"sysfs topology not readable: {type(error).__name__}: {error}"
+        return info
 
 
 def workload_config(args, world):
+    """The workload of the config-2 line; identical in both arms at every N."""
     from lynnreal_omni_b200 import workloads as W
+    from lynnreal_omni_b200.parallel import shard_bounds
+    sizes = sorted({e - s for s, e in (shard_bounds(args.tokens, world, r) for r in range(world))})
     return {
-        "workload": "config2: one Flash-like DiT block, W8A8 projection path",
+        "workload": "config2: one Flash-like DiT block, W8A8 projection path, token rows sharded over the GPUs",
         "model": "Flash-like DiT block (D=6144, 48x128 heads, FFN 24576 GELU-tanh)",
-        "tokens_per_gpu": args.tokens,
-        "global_batch": world,
+        "global_tokens": args.tokens,
+        "tokens_per_gpu": sizes[0] if len(sizes) == 1 else sizes,
+        "global_batch": 1,
         "seq_len": args.tokens,
-        "global_tokens": args.tokens * world,
         "projections": {"qkv": [W.HIDDEN, 3 * W.HIDDEN], "o": [W.HIDDEN, W.HIDDEN],
                         "cross_q": [W.HIDDEN, W.HIDDEN], "cross_kv": [W.TEXT_DIM, 2 * W.HIDDEN],
                         "cross_o": [W.HIDDEN, W.HIDDEN], "up": [W.HIDDEN, W.FFN], "down": [W.FFN, W.HIDDEN]},
         "text_context": [W.TEXT_TOKENS, W.TEXT_DIM],
         "attention": "cores stubbed (self-attn returns V, cross-attn returns Q): out of scope",
-        "parallelism": f"dp{world} (token rows per GPU, int8 weights replicated, no collective)",
-        "l2": "no flush: per-step working set (0.58 GB int8 weights + ~1.2 GB activations) >> 126 MB L2",
+        "parallelism": (f"{world} GPU(s): contiguous token-row shards, int8 weights replicated, "
+                        "one NCCL all_gather_into_tensor of the bf16 block output per step"
+                        if world > 1 else "1 GPU: all token rows, no collective"),
+        "l2": "no flush: per-step working set (0.58 GB int8 weights + activations) >> 126 MB L2",
     }
 
 
@@ -198,79 +219,67 @@ class SmiSampler:
                 "power_w_max": hi}
 
 
-def cpu_block_rate(weights_cpu, tokens: int, sample_rows: int, repeats: int = 3):
-    """Tokens/s of the reference's PyTorch CPU path on this host for a block of
-    `tokens` rows, from a bounded sample: the row-proportional part is timed on
-    `sample_rows` rows and extrapolated linearly; the text K/V projection (fixed
-    per block) is timed in full."""
+def _cpu_times(fn, warmup: int, repeats: int):
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return ts
+
+
+def cpu_block_rate(weights_cpu, tokens: int, repeats: int = 3, extrapolation_rows: int = 512):
+    """Tokens/s of the reference's PyTorch CPU path (oracle/w8a8_torch.py) on
+    this host for the whole block of ``tokens`` rows: one warm-up, median of
+    ``repeats`` timed runs. Beside it, the earlier bounded-sample estimate
+    (``extrapolation_rows`` rows timed, extrapolated linearly) for comparison."""
     from oracle import w8a8_torch as T
     from lynnreal_omni_b200 import block
     torch.set_num_threads(os.cpu_count() or 1)
-    x, table, idx, ctx = block.make_inputs(sample_rows, seed=7)
-    x2 = x.view(sample_rows, -1)
+    x, table, idx, ctx = block.make_inputs(tokens, seed=7)
+    x2 = x.view(tokens, -1)
+    full = statistics.median(_cpu_times(lambda: T.flash_block(x2, table, idx, ctx, weights_cpu), 1, repeats))
 
-    def run_rows():
-        T.flash_block(x2, table, idx, ctx, weights_cpu)
+    xs = x2[:extrapolation_rows].contiguous()
+    ids = idx[:extrapolation_rows].contiguous()
+    t_sample = statistics.median(_cpu_times(lambda: T.flash_block(xs, table, ids, ctx, weights_cpu), 1, repeats))
 
-    def run_fixed():
+    def fixed():
         q, s = T.quantize_rows(ctx)
         T.int8_matmul(q, weights_cpu.cross_kv.weight.t(), s, weights_cpu.cross_kv.scale, weights_cpu.cross_kv.bias)
-
-    def med(fn):
-        fn()
-        ts = []
-        for _ in range(repeats):
-            t0 = time.perf_counter()
-            fn()
-            ts.append(time.perf_counter() - t0)
-        return statistics.median(ts)
-    t_all = med(run_rows)
-    t_fixed = med(run_fixed)
-    t_rows = max(t_all - t_fixed, 1e-9)
-    t_block = t_fixed + t_rows * tokens / sample_rows
-    return tokens / t_block, {"t_sample_s": t_all, "t_fixed_s": t_fixed, "t_block_s": t_block,
-                              "cores": torch.get_num_threads()}
+    t_fixed = statistics.median(_cpu_times(fixed, 1, repeats))
+    t_extrapolated = t_fixed + max(t_sample - t_fixed, 1e-9) * tokens / extrapolation_rows
+    return tokens / full, {"t_block_s": full, "cores": torch.get_num_threads(), "repeats": repeats,
+                           "extrapolated_from_sample": {"rows": extrapolation_rows,
+                                                        "tokens_per_s": tokens / t_extrapolated,
+                                                        "t_block_s": t_extrapolated}}
 
 
 def run_reference(args, world):
-    """Rank 0: the reference's PyTorch CPU path, all host threads, bounded samples."""
+    """Rank 0: the reference's PyTorch CPU path on all host threads; every step
+    is the whole config-2 block (all token rows, unsharded) on the CPU."""
     from oracle import w8a8_torch as T
     from lynnreal_omni_b200 import block
     torch.set_num_threads(os.cpu_count() or 1)
     weights = block.make_weights(seed=0)
-    x, table, idx, ctx = block.make_inputs(args.cpu_sample_rows, seed=7)
-    x2 = x.view(args.cpu_sample_rows, -1)
-
-    def fixed():
-        q, s = T.quantize_rows(ctx)
-        T.int8_matmul(q, weights.cross_kv.weight.t(), s, weights.cross_kv.scale, weights.cross_kv.bias)
-    fixed()
-    tf = []
-    for _ in range(3):
-        t0 = time.perf_counter()
-        fixed()
-        tf.append(time.perf_counter() - t0)
-    t_fixed = statistics.median(tf)
-    for _ in range(args.warmup):
-        T.flash_block(x2, table, idx, ctx, weights)
-    ts = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        T.flash_block(x2, table, idx, ctx, weights)
-        ts.append(time.perf_counter() - t0)
+    x, table, idx, ctx = block.make_inputs(args.tokens, seed=7)
+    x2 = x.view(args.tokens, -1)
+    ts = _cpu_times(lambda: T.flash_block(x2, table, idx, ctx, weights), args.warmup, args.steps)
     t_step = statistics.mean(ts)
-    t_block = t_fixed + max(t_step - t_fixed, 1e-9) * args.tokens / args.cpu_sample_rows
-    value = args.tokens / t_block
+    value = args.tokens / t_step
     cores = torch.get_num_threads()
-    sample = (f"{args.cpu_sample_rows} of {args.tokens} token rows per step (row-proportional part "
-              f"extrapolated linearly to {args.tokens}; text K/V projection timed in full)")
+    sample = (f"every step is the whole block: all {args.tokens} token rows, text K/V projection included "
+              f"(mean of {args.steps} steps after {args.warmup} warm-up)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_block * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": workload_config(args, 1),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": sample,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(args, world),
+        "execution": "rank 0 only, host CPU, all threads, unsharded (the reference has no GPU or multi-process "
+                     "path for this block)",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
                          "implementation": "reference PyTorch path (Int8Linear torch path + torch restatement "
                                            "of the Triton kernels), oracle/w8a8_torch.py"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -278,10 +287,35 @@ def run_reference(args, world):
     print(json.dumps(line), flush=True)
 
 
+def int8_ceiling_cublaslt(m: int, k: int, n: int, dev, reps: int = 10) -> float:
+    """Measured int8 tensor ceiling on this GPU: cuBLASLt ``torch._int_mm`` at
+    the dominant kernel's shape (int32 output, no epilogue), TOP/s over
+    ``reps`` back-to-back launches after warm-up, CUDA events."""
+    g = torch.Generator(device=dev).manual_seed(5)
+    mp = max(32, -(-m // 8) * 8)
+    a = torch.randint(-127, 128, (mp, k), generator=g, device=dev, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        torch._int_mm(a, b)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / reps
+    del a, b
+    return 2.0 * m * n * k / (ms / 1e3) / 1e12
+
+
 def run_ours(args, rank, world, local):
+    """Config 2: one block over ``args.tokens`` token rows, sharded into
+    contiguous row blocks over the ranks; every step ends with the NCCL
+    all-gather of the bf16 block output, inside the timed region."""
     import torch.distributed as dist
     from lynnreal_omni_b200 import block, _lib
     from lynnreal_omni_b200 import workloads as W
+    from lynnreal_omni_b200.parallel import RowGather, shard_bounds
 
     if not torch.cuda.is_available():
         raise RuntimeError("bench.py needs a CUDA GPU")
@@ -292,75 +326,142 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load()
 
+    total, d = args.tokens, W.HIDDEN
+    start_row, stop_row = shard_bounds(total, world, rank)
+    m = stop_row - start_row
     weights = block.make_weights(seed=0, device=dev)  # replicated: same seed on every rank
     blk = block.FlashBlockW8A8(weights)
-    x, table, idx, ctx = block.make_inputs(args.tokens, seed=100 + rank, device=dev)
+    x_full, table, idx_full, ctx = block.make_inputs(total, seed=100, device=dev)  # same latent on every rank
+    x = x_full[:, start_row:stop_row].contiguous()
+    idx = idx_full[start_row:stop_row].contiguous()
+    gather = RowGather(total) if world > 1 else None
+    out_buf = torch.empty(total, d, dtype=torch.bfloat16, device=dev) if gather else None
     torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    def step(xin, ffn_ev=None, ag_ev=None, out=None):
+        h, _ = blk(xin, table, idx, ctx, ffn_events=ffn_ev)
+        if gather is None:
+            return h.view(m, d)
+        if ag_ev is not None:
+            ag_ev[0].record()
+        res = gather(h.view(m, d), out)
+        if ag_ev is not None:
+            ag_ev[1].record()
+        return res
+
     for _ in range(args.warmup):
-        blk(x, table, idx, ctx)
+        step(x, out=out_buf)
     torch.cuda.synchronize()
 
     sampler = clock_sampler(dev, local) if rank == 0 else None
     if sampler:
         sampler.start()
-    ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))  # noqa: E731
+    ffn = [ev() for _ in range(args.steps)]
+    ag = [ev() for _ in range(args.steps)]
+    start, end = ev()
     barrier()
     torch.cuda.synchronize()
     start.record()
     for i in range(args.steps):
-        blk(x, table, idx, ctx, ffn_events=ffn[i])
+        out = step(x, ffn[i], ag[i], out_buf)
     end.record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
     elapsed_ms = start.elapsed_time(end)
     ffn_ms = statistics.mean(a.elapsed_time(b) for a, b in ffn)
-    t = torch.tensor([elapsed_ms, ffn_ms], device=dev, dtype=torch.float64)
+    ag_ms = statistics.mean(a.elapsed_time(b) for a, b in ag) if gather else 0.0
+    t = torch.tensor([elapsed_ms, ffn_ms, ag_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, ffn_ms = t.tolist()
+    elapsed_ms, ffn_ms, ag_ms = t.tolist()
     status = _lib.device_status(clear=True)
 
-    # end to end through the public API: every step copies its latent and text
-    # context from pinned host memory and its result back to pinned host memory;
-    # HostPipeline overlaps step i's compute with the copies of steps i+1 / i-1.
+    # the gathered rows equal the unsharded block (rows are independent)
+    gathered_ok = None
+    if gather is not None:
+        ok = torch.tensor([1], device=dev)
+        if rank == 0:
+            ok[0] = int(torch.equal(out, blk(x_full, table, idx_full, ctx)[0].view(total, d)))
+        dist.broadcast(ok, 0)
+        gathered_ok = bool(ok.item())
+        torch.cuda.synchronize()
+
+    # weak-scaling replica figure (each rank the whole latent, no collective): an extra key
+    replica = None
+    if world > 1:
+        reps = max(3, min(args.steps, 10))
+        for _ in range(2):
+            blk(x_full, table, idx_full, ctx)
+        r0, r1 = ev()
+        barrier()
+        torch.cuda.synchronize()
+        r0.record()
+        for _ in range(reps):
+            blk(x_full, table, idx_full, ctx)
+        r1.record()
+        torch.cuda.synchronize()
+        barrier()
+        tr = torch.tensor([r0.elapsed_time(r1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(tr, op=dist.ReduceOp.MAX)
+        replica = {"tokens_per_s": world * total * reps / (tr.item() / 1e3), "steps": reps,
+                   "what": f"each of the {world} ranks runs all {total} rows, no collective (weak scaling)"}
+
+    # end to end through the public API: every step copies this rank's latent
+    # shard and the text context from pinned host memory, runs the block,
+    # all-gathers the output and reads this rank's row range of the gathered
+    # output back to pinned host memory (the ranks together read the whole
+    # output once); HostPipeline overlaps step i's compute with the copies of
+    # steps i+1 / i-1.
     e2e = None
     if not args.no_e2e:
         from lynnreal_omni_b200.pipeline import HostPipeline
         x_h = [x.cpu().pin_memory() for _ in range(2)]
         ctx_h = ctx.cpu().pin_memory()
-        out_h = [torch.empty_like(x_h[0]).pin_memory() for _ in range(2)]
-        pipe = HostPipeline(lambda xd, cd: blk(xd, table, idx, cd)[0], dev, [x_h[0], ctx_h])
+        out_h = [torch.empty(m, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+
+        def api(xd, cd):
+            h, _ = blk(xd, table, idx, cd)
+            if gather is None:
+                return h.view(m, d)
+            return gather(h.view(m, d))[start_row:stop_row]  # fresh buffer per step: read while the next runs
+        pipe = HostPipeline(api, dev, [x_h[0], ctx_h])
         ins = [[x_h[i & 1], ctx_h] for i in range(args.steps)]
         outs = [out_h[i & 1] for i in range(args.steps)]
         pipe.run(ins[:2], outs[:2])
         torch.cuda.synchronize()
         barrier()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2, e2 = ev()
         s2.record()
         pipe.run(ins, outs)
         e2.record()
         torch.cuda.synchronize()
         barrier()
-        ok = torch.equal(out_h[(args.steps - 1) & 1], blk(x, table, idx, ctx)[0].cpu())
+        ok = torch.equal(out_h[(args.steps - 1) & 1], out[start_row:stop_row].cpu() if gather else out.cpu())
         te = torch.tensor([s2.elapsed_time(e2)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = te.item()
-        e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+        e2e = {"value": total * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": x_h[0].numel() * 2 + ctx_h.numel() * 2,
-               "d2h_bytes_per_step": out_h[0].numel() * 2, "ms_per_step": e2e_ms / args.steps,
+               "d2h_bytes_per_step": out_h[0].numel() * 2,
+               "bytes_per_step_are": "per rank (this rank's shard in, its row range of the gathered output out)",
+               "h2d_bytes_per_step_all_ranks": total * d * 2 + world * ctx_h.numel() * 2,
+               "d2h_bytes_per_step_all_ranks": total * d * 2,
+               "ms_per_step": e2e_ms / args.steps,
                "result_matches_device_path": ok,
                "api": "HostPipeline over FlashBlockW8A8.forward (Int8Linear / kernels / int8_gemm over "
-                      "liblr_w8a8.so); pinned host input and output every step, copies overlapped with compute"}
+                      "liblr_w8a8.so) + parallel.RowGather; pinned host input and output every step, copies "
+                      "overlapped with compute"}
 
+    ceiling = None
+    if rank == 0:
+        ceiling = int8_ceiling_cublaslt(m, W.HIDDEN, W.FFN, dev)
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -372,40 +473,51 @@ def run_ours(args, rank, world, local):
     peaks = measured_peaks()
     bf16_burst = peaks.get("bf16_tflops")
     peak = 2.0 * (bf16_burst if bf16_burst else FALLBACK_BF16_BURST_TFLOPS)
-    up_ops = 2.0 * args.tokens * W.FFN * W.HIDDEN
+    up_ops = 2.0 * m * W.FFN * W.HIDDEN
     achieved = up_ops / (ffn_ms / 1e3) / 1e12
     roofline = {
         "kernel": "ffn_up int8 GEMM + GELU-tanh epilogue (CTA-pair gemm_tc2_kernel<kGelu>), "
-                  f"M={args.tokens} K={W.HIDDEN} N={W.FFN}",
+                  f"M={m} K={W.HIDDEN} N={W.FFN}",
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s (int8)",
         "frac": achieved / peak,
         "peak_source": ("of measured: 2 x bf16_tflops burst in MEASURED_PEAKS.json (B200 dense int8 = 2 x bf16 "
                         "per clock)" if bf16_burst else "of fallback: 2 x 1590 TFLOP/s bf16 burst"),
+        "peak_int8_cublaslt_measured": ceiling,
+        "frac_of_cublaslt_measured": achieved / ceiling if ceiling else None,
+        "cublaslt_note": "torch._int_mm (cuBLASLt, int32 out, no epilogue) at the same shape on this GPU, this run",
         "peak_int8_at_sm_clock": 148 * 16384 * (clocks["sm_mhz"] if clocks and clocks.get("sm_mhz") else 1965.0)
         * 1e6 / 1e12,
         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
         "algorithmic_ops_per_launch": up_ops,
         "launch_ms": ffn_ms,
-        "traffic": profile_traffic("gemm_ffn_up_m12240"),
+        "traffic": profile_traffic("gemm_ffn_up_m12240") if m == 12240 else None,
     }
-    block_ops = 2.0 * args.tokens * W.HIDDEN * (3 * W.HIDDEN + 3 * W.HIDDEN + 2 * W.FFN) \
-        + 2.0 * W.TEXT_TOKENS * W.TEXT_DIM * 2 * W.HIDDEN
+    block_ops = 2.0 * total * W.HIDDEN * (3 * W.HIDDEN + 3 * W.HIDDEN + 2 * W.FFN) \
+        + 2.0 * world * W.TEXT_TOKENS * W.TEXT_DIM * 2 * W.HIDDEN
     step_ms = elapsed_ms / args.steps
     line = {
         "metric": METRIC,
-        "value": world * args.tokens * args.steps / (elapsed_ms / 1e3),
+        "value": total * args.steps / (elapsed_ms / 1e3),
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": step_ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded; random-init int8 weights)",
         "config": workload_config(args, world),
         "block_tops": block_ops / (step_ms / 1e3) / 1e12,
+        "allgather": None if gather is None else {
+            "ms_per_step": ag_ms, "share_of_step": ag_ms / step_ms,
+            "bytes_received_per_rank": (total - m) * d * 2,
+            "algbw_GBps": total * d * 2 / (ag_ms / 1e3) / 1e9,
+            "busbw_GBps": (world - 1) / world * total * d * 2 / (ag_ms / 1e3) / 1e9,
+            "gathered_matches_unsharded": gathered_ok,
+            "timing": "CUDA events around all_gather_into_tensor on the compute stream, mean over steps, max over ranks"},
+        "replica": replica,
         "roofline": roofline,
         "clocks": clocks,
         "gpu_launches": block.LAUNCHES_PER_FORWARD * args.steps,
@@ -415,15 +527,16 @@ def run_ours(args, rank, world, local):
     if world == 1 and not args.no_cpu_baseline:
         wcpu = block.BlockWeights(**{k: (v.to("cpu") if hasattr(v, "to") else v)
                                      for k, v in weights.__dict__.items()})
-        rate, info = cpu_block_rate(wcpu, args.tokens, args.cpu_sample_rows)
+        rate, info = cpu_block_rate(wcpu, total)
         line["cpu_baseline"] = {
             "value": rate, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
-            "sample": (f"{args.cpu_sample_rows} of {args.tokens} token rows (row-proportional part "
-                       f"extrapolated linearly; text K/V projection timed in full)"),
+            "sample": (f"the whole block: all {total} token rows, median of {info['repeats']} runs after one "
+                       "warm-up"),
             "t_block_s": info["t_block_s"],
+            "extrapolated_from_sample": info["extrapolated_from_sample"],
         }
     if isinstance(line.get("e2e"), dict):
-        line["e2e"]["host_numa_node"] = numa
+        line["e2e"]["host_numa"] = numa
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -562,7 +675,7 @@ def run_stack(args, rank, world, local):
                     "ms_per_step": te.item() / args.steps},
         }
         if isinstance(line.get("e2e"), dict):
-            line["e2e"]["host_numa_node"] = numa
+            line["e2e"]["host_numa"] = numa
         print(json.dumps(line), flush=True)
     del out
     if world > 1:
@@ -764,7 +877,7 @@ def run_flash(args, rank, world, local):
                     "ms_per_step": te.item() / args.steps},
         }
         if isinstance(line.get("e2e"), dict):
-            line["e2e"]["host_numa_node"] = numa
+            line["e2e"]["host_numa"] = numa
         print(json.dumps(line), flush=True)
     del out
     if world > 1:

@@ -94,13 +94,19 @@ class FlashBlockW8A8:
         return int8_matmul_gated_residual(q, layer.weight_int8, s, layer.weight_scale, layer.bias, residual,
                                           table, idx, slot, out=out)
 
-    def forward(self, x, table, indices, context, ffn_events=None):
+    def forward(self, x, table, indices, context, ffn_events=None, probe=None):
         """x bf16 [1, M, D] -> (x' bf16 [1, M, D], text K/V bf16 [T, 2D]).
 
         ``ffn_events`` (start, end) CUDA events, if given, bracket the FFN-up
-        GEMM launch (the dominant kernel) on the current stream.
+        GEMM launch (the dominant kernel) on the current stream. ``probe``, if
+        given, is called as ``probe(stage, tensor)`` with the block's
+        intermediate results in stream order: "attn" (x after the O projection
+        and its gated residual), "cross" (after the cross-attention residual),
+        "ffn_up" (the GELU-tanh output [M, FFN]). The residual stream is then
+        updated in place, so a probe that keeps a tensor must copy it.
         """
         d = self.hidden
+        note = probe or (lambda stage, t: None)
         m = x.shape[-2]
         # self-attention: adaLN prologue (slots 0, 1) -> fused QKV
         q, s = K._rms_adaln_quant_int8(x, self.norm1, table, indices, 0, 1)
@@ -108,6 +114,7 @@ class FlashBlockW8A8:
         attn = qkv[:, 2 * d:]  # attention stub: output := V
         q, s = K.quantize_rows(attn)
         h = self._gated(self.o, q, s, x, table, indices, 2)  # O-proj + gated residual (slot 2)
+        note("attn", h)
         # cross-attention: slot-free RMSNorm prologue -> Q; text K/V from the context
         q, s = K._rms_adaln_quant_int8(h, self.norm_cross, None, None, 0, 0)
         cq = self.cross_q.forward_quantized(q, s, (m,))
@@ -115,6 +122,7 @@ class FlashBlockW8A8:
         kv = self.cross_kv.forward_quantized(cq8, cs, (context.shape[0],))
         q, s = K.quantize_rows(cq)  # cross-attention stub: output := its query projection
         self._gated(self.cross_o, q, s, h, None, None, 0, out=h)  # cross-O + plain residual, in place
+        note("cross", h)
         # FFN: adaLN prologue (slots 3, 4) -> up + GELU-tanh -> quant -> down + gated residual (slot 5)
         q, s = K._rms_adaln_quant_int8(h, self.norm2, table, indices, 3, 4)
         if ffn_events is not None:
@@ -122,6 +130,7 @@ class FlashBlockW8A8:
         u = int8_matmul_gelu(q, self.up.weight_int8, s, self.up.weight_scale, self.up.bias)
         if ffn_events is not None:
             ffn_events[1].record()
+        note("ffn_up", u)
         q, s = K.quantize_rows(u)
         self._gated(self.down, q, s, h, table, indices, 5, out=h)
         return h, kv

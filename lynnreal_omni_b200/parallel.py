@@ -37,27 +37,55 @@ def frame_bounds(frames: int, frame_rows: int, world: int, rank: int) -> tuple[i
     return f0 * frame_rows, f1 * frame_rows
 
 
+class RowGather:
+    """All-gather of every rank's row block into the full ``[total, ...]`` tensor.
+
+    Built once per (total, bounds): equal shards (12240 rows over 1/2/4/8 GPUs,
+    for instance) are gathered straight from ``local`` into the output with one
+    ``all_gather_into_tensor``; unequal shards go through a padded staging
+    buffer and are compacted afterwards. ``out``, if given, receives the rows
+    (equal shards only need no copy at all).
+    """
+
+    def __init__(self, total: int, group=None, bounds=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.total = total
+        self.bounds = bounds or [shard_bounds(total, self.world, r) for r in range(self.world)]
+        b = self.bounds
+        if len(b) != self.world or b[0][0] != 0 or b[-1][1] != total or any(
+                b[r][1] != b[r + 1][0] for r in range(self.world - 1)):
+            raise ValueError("row bounds must tile [0, total) in rank order")
+        self.width = max(e - s for s, e in b)
+        self.even = all(e - s == self.width for s, e in b)
+
+    def __call__(self, local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        start, stop = self.bounds[self.rank]
+        if local.shape[0] != stop - start:
+            raise ValueError(f"rank {self.rank} holds {local.shape[0]} rows, expected {stop - start}")
+        shape = (self.total, *local.shape[1:])
+        if out is not None and (tuple(out.shape) != shape or out.dtype != local.dtype or not out.is_contiguous()):
+            raise ValueError(f"gather output must be a contiguous {local.dtype} tensor of shape {shape}")
+        if self.even:
+            out = local.new_empty(shape) if out is None else out
+            dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+            return out
+        padded = local.new_zeros((self.width, *local.shape[1:]))
+        padded[: local.shape[0]] = local
+        staged = local.new_empty((self.world * self.width, *local.shape[1:]))
+        dist.all_gather_into_tensor(staged, padded, group=self.group)
+        parts = [staged[r * self.width: r * self.width + (e - s)] for r, (s, e) in enumerate(self.bounds)]
+        if out is None:
+            return torch.cat(parts, dim=0)
+        return torch.cat(parts, dim=0, out=out)
+
+
 def gather_rows(local: torch.Tensor, total: int, group=None, bounds=None) -> torch.Tensor:
     """All-gather the row blocks of every rank into the full [total, ...] tensor.
 
     ``local`` is this rank's block (rows on dim 0); ``bounds[r]`` is rank r's
-    [start, stop) (default: ``shard_bounds``). One all_gather_into_tensor of
-    equally padded shards; the result is identical on every rank.
+    [start, stop) (default: ``shard_bounds``). The result is identical on every
+    rank (see ``RowGather``).
     """
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    bounds = bounds or [shard_bounds(total, world, r) for r in range(world)]
-    if len(bounds) != world or bounds[0][0] != 0 or bounds[-1][1] != total or any(
-            bounds[r][1] != bounds[r + 1][0] for r in range(world - 1)):
-        raise ValueError("row bounds must tile [0, total) in rank order")
-    start, stop = bounds[rank]
-    if local.shape[0] != stop - start:
-        raise ValueError(f"rank {rank} holds {local.shape[0]} rows, expected {stop - start}")
-    width = max(e - s for s, e in bounds)
-    padded = local.new_zeros((width, *local.shape[1:]))
-    padded[: local.shape[0]] = local
-    out = local.new_empty((world * width, *local.shape[1:]))
-    dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
-    if all(e - s == width for s, e in bounds):
-        return out
-    return torch.cat([out[r * width: r * width + (e - s)] for r, (s, e) in enumerate(bounds)], dim=0)
+    return RowGather(total, group, bounds)(local)

@@ -110,11 +110,17 @@ def gated_residual(x, y, table=None, indices=None, gate_slot=0, sequence=None):
     return bf(x + bf(gate * y))
 
 
-def flash_block(x, table, indices, context, w, reduce=sumsq_quant):
+def flash_block(x, table, indices, context, w, reduce=sumsq_quant, stages=None, gelu_out=None):
     """The benchmark block's W8A8 path (lynnreal_omni_b200/block.py) on the CPU.
 
     x: bf16/fp32 [M, D]; w: a BlockWeights on the CPU. Returns (x' float32
-    [M, D] of bf16 values, text K/V float32 [T, 2D])."""
+    [M, D] of bf16 values, text K/V float32 [T, 2D]). The kernel order is the
+    reference's fused block (model/fusion.py:61-98) with the benchmark's
+    cross-attention and GELU FFN. ``stages`` (a dict), if given, receives the
+    intermediates "attn", "cross" and "ffn_up" (the GELU-tanh output).
+    ``gelu_out`` [M, FFN], if given, replaces this port's GELU-tanh output in
+    the FFN-down step, so that step can be checked exactly against a device
+    whose tanh differs in the last bit."""
     d = x.shape[-1]
     lin = lambda p, q, s: int8_matmul(q, p.weight.t(), s, p.scale, p.bias)  # noqa: E731
     h = x.to(F32)
@@ -122,14 +128,20 @@ def flash_block(x, table, indices, context, w, reduce=sumsq_quant):
     qkv = lin(w.qkv, q, s)
     q, s = quantize_rows(qkv[:, 2 * d:])
     h = gated_residual(h, lin(w.o, q, s), table, indices, 2)
+    if stages is not None:
+        stages["attn"] = h
     q, s = quantize_rows(rms_adaln(h, w.norm_cross, w.eps, reduce=reduce))
     cq = lin(w.cross_q, q, s)
     c8, cs = quantize_rows(context)
     kv = lin(w.cross_kv, c8, cs)
     q, s = quantize_rows(cq)
     h = gated_residual(h, lin(w.cross_o, q, s))
+    if stages is not None:
+        stages["cross"] = h
     q, s = quantize_rows(rms_adaln(h, w.norm2, w.eps, table, indices, 3, 4, reduce=reduce))
     u = gelu_tanh_bf16(lin(w.up, q, s))
-    q, s = quantize_rows(u)
+    if stages is not None:
+        stages["ffn_up"] = u
+    q, s = quantize_rows(u if gelu_out is None else gelu_out.to(F32))
     h = gated_residual(h, lin(w.down, q, s), table, indices, 5)
     return h, kv
