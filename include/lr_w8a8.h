@@ -70,6 +70,12 @@ int lr_device_status(unsigned int* bits, int clear);
  * columns). Set it before launching work on the device. */
 #define LR_ARITH_IEEE 0
 #define LR_ARITH_REFERENCE_GPU 1
+/* LR_ARITH_TORCH_CUDA (lr_quantize_rows_arith only): the reference's unfused
+ * PyTorch quantiser as it runs on a CUDA device (Int8Linear.forward with
+ * fused_ops off, model/int8.py:66-67). PyTorch divides a CUDA tensor by a
+ * scalar as a multiply by the float reciprocal, so
+ *   scale = fl(max(absmax, 1e-8) * fl(1/127)),  q = RNE(clamp(x / scale)) (IEEE /). */
+#define LR_ARITH_TORCH_CUDA 2
 int lr_set_arithmetic(int mode);
 int lr_get_arithmetic(int* mode);
 
@@ -82,6 +88,12 @@ int lr_get_arithmetic(int* mode);
  * q: int8 [rows, width] contiguous; scales: fp32 [rows]. */
 int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
                      int8_t* q, float* scales, void* stream);
+
+/* K1 with the arithmetic chosen per call instead of the device's mode:
+ * LR_ARITH_IEEE, LR_ARITH_REFERENCE_GPU or LR_ARITH_TORCH_CUDA. Int8Linear's
+ * unfused quantiser (model/int8.py:66-67) runs as LR_ARITH_TORCH_CUDA. */
+int lr_quantize_rows_arith(const void* x, int64_t rows, int64_t width, int64_t row_stride,
+                           int8_t* q, float* scales, int arithmetic, void* stream);
 
 /* K2 — standalone int32 -> bf16 dequant epilogue.
  * Replaces model/kernels.py:41-46 `int8_epilogue` (kernel :27-38), used by
@@ -212,8 +224,8 @@ int lr_attention_bf16(const void* q, int64_t q_token_stride, const void* k, int6
                       void* stream);
 
 /* K10 (+K2 fused) — INT8 GEMM with int32 accumulation and a fused bf16 epilogue.
- * Replaces model/int8_gemm.py:200-267 `int8_matmul` (kernel `_gemm` :117-150),
- * model/int8_tma.py:299-308 `matmul`, and the GEMM inside
+ * Replaces model/int8_gemm.py:96-163 `int8_matmul` (kernel `_gemm` :13-46),
+ * model/int8_tma.py:32-41 `matmul`, and the GEMM inside
  * Int8Linear.forward_quantized (model/int8.py:41-58).
  *   acc[m,n] = sum_k a[m,k] * b[k,n]                       (exact int32)
  *   d[m,n]   = (float(acc) * row_scale[m]) * col_scale[n] (+ bias[n])

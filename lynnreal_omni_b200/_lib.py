@@ -37,6 +37,7 @@ SIGNATURES = {
     "lr_set_arithmetic": ([_i32], _i32),
     "lr_get_arithmetic": ([ctypes.POINTER(ctypes.c_int)], _i32),
     "lr_quantize_rows": ([_p, _i64, _i64, _i64, _p, _p, _p], _i32),
+    "lr_quantize_rows_arith": ([_p, _i64, _i64, _i64, _p, _p, _i32, _p], _i32),
     "lr_int8_epilogue": ([_p, _i64, _i64, _p, _p, _p, _p, _p], _i32),
     "lr_rms_adaln": ([_p, _p, _f32, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _i32, _p, _p], _i32),
     "lr_rms_adaln_quant_int8": ([_p, _p, _f32, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _i32,
@@ -116,6 +117,9 @@ def stream_of(tensor: torch.Tensor) -> int:
 
 
 ARITHMETIC = {"reference_gpu": 1, "ieee": 0}
+# per-call quantiser arithmetic only (lr_quantize_rows_arith): the reference's
+# unfused PyTorch quantiser on a CUDA device
+LR_ARITH_TORCH_CUDA = 2
 
 
 def set_arithmetic(mode: str) -> None:

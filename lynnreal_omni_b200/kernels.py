@@ -45,11 +45,15 @@ def _adaln(table: torch.Tensor, indices: torch.Tensor, device: torch.device, seq
     return table, rows, width, idx
 
 
-def quantize_rows(value: torch.Tensor):
+def quantize_rows(value: torch.Tensor, *, arithmetic: str | None = None):
     """Per-row int8 quantisation -> (int8 [rows, width], fp32 [rows, 1]).
 
     Replaces model/kernels.py:19-24. Rows may be strided (unit column stride);
     e.g. a column slice of a fused QKV output is quantised in place.
+    ``arithmetic`` (keyword only, not in the reference's signature) overrides
+    the device's arithmetic mode for this call: "reference_gpu", "ieee" or
+    "torch_cuda" (the reference's unfused PyTorch quantiser on a CUDA device,
+    model/int8.py:66-67: scale = absmax x fl(1/127), IEEE quotient).
     """
     rows, width = value.shape
     _require_bf16("quantize_rows", value)
@@ -57,8 +61,17 @@ def quantize_rows(value: torch.Tensor):
         value = value.contiguous()
     output = torch.empty((rows, width), device=value.device, dtype=torch.int8)
     scales = torch.empty(rows, 1, device=value.device, dtype=torch.float32)
-    check(_lib.load().lr_quantize_rows(ptr(value), rows, width, value.stride(0) if rows > 1 else width,
-                                       ptr(output), ptr(scales), stream_of(value)), "quantize_rows")
+    stride = value.stride(0) if rows > 1 else width
+    if arithmetic is None:
+        status = _lib.load().lr_quantize_rows(ptr(value), rows, width, stride, ptr(output), ptr(scales),
+                                              stream_of(value))
+    else:
+        modes = dict(_lib.ARITHMETIC, torch_cuda=_lib.LR_ARITH_TORCH_CUDA)
+        if arithmetic not in modes:
+            raise ValueError(f"quantize_rows: arithmetic must be one of {sorted(modes)}, got {arithmetic!r}")
+        status = _lib.load().lr_quantize_rows_arith(ptr(value), rows, width, stride, ptr(output), ptr(scales),
+                                                    modes[arithmetic], stream_of(value))
+    check(status, "quantize_rows")
     return output, scales
 
 

@@ -90,18 +90,22 @@ def _factory(config):
 def test_load_transformer_installs_packed_layers_and_fuses_qkv(tmp_path):
     tensors = _write_checkpoint(tmp_path)
     model = flash_int8.load_transformer(tmp_path, device="cpu", gemm="torch", model_factory=_factory)
-    x = torch.randn(5, D).to(torch.bfloat16)
     for i, block in enumerate(model.transformer_blocks):
         attn = block.attn
         assert attn.to_q is None and attn.to_k is None and attn.to_v is None and attn.fused_projections
         assert isinstance(attn.to_qkv, Int8Linear) and isinstance(attn.to_out[0], Int8Linear)
-        separate = []
-        for name in ("to_q", "to_k", "to_v"):
-            key = f"transformer_blocks.{i}.attn.{name}"
-            layer = Int8Linear.from_packed(tensors[key + ".weight_int8"], tensors[key + ".weight_scale"],
-                                           tensors.get(key + ".bias"), gemm="torch")
-            separate.append(layer(x))
-        assert torch.equal(attn.to_qkv(x), torch.cat(separate, dim=-1))
+        # the fused QKV holds the Q, K, V rows, scales and biases in that order
+        # (its projection then equals the three separate ones row for row)
+        keys = [f"transformer_blocks.{i}.attn.{name}" for name in ("to_q", "to_k", "to_v")]
+        rows = torch.cat([tensors[k + ".weight_int8"] for k in keys])
+        scales = torch.cat([tensors[k + ".weight_scale"] for k in keys])
+        assert torch.equal(attn.to_qkv.weight_int8.t(), rows)
+        assert torch.equal(attn.to_qkv.weight_scale.t(), scales)
+        biases = [tensors.get(k + ".bias") for k in keys]
+        if any(b is not None for b in biases):
+            expect = torch.cat([b if b is not None else torch.zeros(rows.shape[0] // 3, dtype=torch.bfloat16)
+                                for b in biases])
+            assert torch.equal(attn.to_qkv.bias, expect)
         assert torch.equal(block.scale_shift_table, tensors[f"transformer_blocks.{i}.scale_shift_table"])
     assert torch.equal(model.proj_out.weight, tensors["proj_out.weight"])
     assert not model.training
@@ -135,6 +139,27 @@ def test_fuse_qkv_without_biases():
         parts.append(Int8Linear.from_packed(w, s, None, gemm="torch"))
     attn.to_q, attn.to_k, attn.to_v = parts
     flash_int8.fuse_qkv(SimpleNamespace(transformer_blocks=[SimpleNamespace(attn=attn)]), gemm="torch")
-    x = torch.randn(3, D).to(torch.bfloat16)
     assert attn.to_qkv.bias is None
-    assert torch.equal(attn.to_qkv(x), torch.cat([p(x) for p in parts], dim=-1))
+    assert torch.equal(attn.to_qkv.weight_int8.t(), torch.cat([p.weight_int8.t() for p in parts]))
+    assert torch.equal(attn.to_qkv.weight_scale, torch.cat([p.weight_scale for p in parts], dim=1))
+
+
+@pytest.mark.gpu
+def test_fused_qkv_projects_like_the_three_layers_on_gpu():
+    """On the GPU the fused QKV layer's output equals the separate Q, K, V
+    projections concatenated (model/flash_int8.py:47-55)."""
+    attn = SimpleNamespace(to_q=None, to_k=None, to_v=None, fused_projections=False)
+    g = torch.Generator().manual_seed(4)
+    parts = []
+    for with_bias in (True, False, True):
+        w = torch.randint(-127, 128, (D, D), generator=g, dtype=torch.int8)
+        s = torch.empty(D, 1).uniform_(0.5e-3, 2e-3, generator=g)
+        b = (0.02 * torch.randn(D, generator=g)).to(torch.bfloat16) if with_bias else None
+        parts.append(Int8Linear.from_packed(w.cuda(), s.cuda(), None if b is None else b.cuda(), gemm="torch"))
+    attn.to_q, attn.to_k, attn.to_v = parts
+    flash_int8.fuse_qkv(SimpleNamespace(transformer_blocks=[SimpleNamespace(attn=attn)]), gemm="torch")
+    x = torch.randn(37, D, generator=g).to(torch.bfloat16).cuda()
+    for fused in (False, True):
+        for layer in parts + [attn.to_qkv]:
+            layer.fused_ops = fused
+        assert torch.equal(attn.to_qkv(x), torch.cat([p(x) for p in parts], dim=-1))

@@ -26,6 +26,7 @@ from lynnreal_omni_b200.int8 import Int8Linear
 from lynnreal_omni_b200.int8_gemm import (int8_matmul, int8_matmul_gated_residual, int8_matmul_gelu,
                                           int8_matmul_s32, _torch_matmul)
 from lynnreal_omni_b200 import int8_tma
+from lynnreal_omni_b200.kernels import quantize_rows
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -138,7 +139,7 @@ def test_matches_reference_cublaslt_path():
 
 
 def test_kat_fingerprints():
-    """The reference's install-time shapes (script/precompile.py:376) hash to the
+    """The reference's install-time shapes (script/precompile.py:50-64) hash to the
     reference's own outputs."""
     fps = json.loads((GOLDEN / "fingerprints.json").read_text())
     for key, fp in fps.items():
@@ -159,19 +160,33 @@ def test_config0_linear_fingerprint():
     assert sha(layer(x.to(DEV))) == fp["sha256"]
 
 
-def test_unfused_quantiser_path_uses_the_same_gemm():
-    """With fused_ops off, Int8Linear quantises with torch ops on the GPU (as the
-    reference does); PyTorch divides by the scalar 127 on CUDA as a multiply by
-    its reciprocal, so those scales are not the CPU's bit for bit. The GEMM
-    behind it is still exact: the output equals the reference's cuBLASLt path
-    on the same quantised rows."""
+@pytest.mark.parametrize("gemm", ["torch", "triton", "b200"])
+def test_unfused_quantiser_path_matches_reference_torch_ops(gemm):
+    """With fused_ops off, the reference quantises with PyTorch ops on the GPU
+    (model/int8.py:66-67; PyTorch divides by the scalar 127 as a multiply by
+    its float reciprocal on CUDA) and runs cuBLASLt plus a torch epilogue.
+    This build runs its CUDA quantiser in that arithmetic and the tcgen05 GEMM,
+    for every backend name: the output equals the reference's path bit for bit."""
     x, pl = workloads.config0(seed=5, m=300, k=6144, n=1024)
-    layer = Int8Linear.from_packed(pl.weight.to(DEV), pl.scale.to(DEV), pl.bias.to(DEV), gemm="triton")
+    layer = Int8Linear.from_packed(pl.weight.to(DEV), pl.scale.to(DEV), pl.bias.to(DEV), gemm=gemm)
     flat = x.to(DEV)
     scale = flat.float().abs().amax(-1, keepdim=True).clamp_min_(1e-8) / 127
     q = (flat.float() / scale).round().clamp(-127, 127).to(torch.int8)
+    got_q, got_s = quantize_rows(flat, arithmetic="torch_cuda")
+    assert torch.equal(got_q, q) and torch.equal(got_s, scale)
     expect = _torch_matmul(q, layer.weight_int8, scale, layer.weight_scale, layer.bias)
     assert torch.equal(layer(flat), expect)
+
+
+@pytest.mark.reference_gpu_arith
+def test_fused_quantiser_route_uses_device_arithmetic():
+    """fused_ops on: the quantiser runs in the device's mode (by default the
+    reference's compiled-kernel arithmetic), as kernels.quantize_rows does."""
+    x, pl = workloads.config0(seed=6, m=257, k=6144, n=512)
+    layer = Int8Linear.from_packed(pl.weight.to(DEV), pl.scale.to(DEV), pl.bias.to(DEV), gemm="torch")
+    layer.fused_ops = True
+    q, s = quantize_rows(x.to(DEV))
+    assert torch.equal(layer(x.to(DEV)), int8_matmul(q, layer.weight_int8, s, layer.weight_scale, layer.bias))
 
 
 def test_torch_backend_with_fused_epilogue():

@@ -101,17 +101,33 @@ def test_int8_linear_contract():
     assert not layer.fused_ops
 
 
-def test_int8_linear_torch_backend_on_cpu_matches_oracle():
-    """gemm="torch" is the reference's own path; it runs on the CPU too."""
-    import numpy as np
-    from oracle import w8a8_oracle as O
+def test_int8_linear_has_no_cpu_path():
+    """Every backend name runs the sm_100a kernels; a CPU tensor is refused
+    instead of being computed by another implementation."""
     from lynnreal_omni_b200 import workloads
     x, pl = workloads.config0(seed=8, m=21, k=256, n=72)
-    layer = Int8Linear.from_packed(pl.weight, pl.scale, pl.bias, gemm="torch")
-    y = layer(x.view(1, 21, 256))
-    ref = O.int8_linear_forward(O.to_numpy_f32(x), pl.weight.numpy(), pl.scale.numpy(), O.to_numpy_f32(pl.bias))
-    assert y.shape == (1, 21, 72)
-    np.testing.assert_array_equal(O.bf16_bits(O.to_numpy_f32(y).reshape(21, 72)), O.bf16_bits(ref))
+    for gemm in ("torch", "triton", "b200"):
+        layer = Int8Linear.from_packed(pl.weight, pl.scale, pl.bias, gemm=gemm)
+        for fused in (False, True):
+            layer.fused_ops = fused
+            with pytest.raises(ValueError):
+                layer(x.view(1, 21, 256))
+
+
+def test_int8_linear_weight_quantisation_matches_reference_golden():
+    """Int8Linear(nn.Linear) stores the reference's int8 rows and scales
+    (golden vectors of model/int8.py:7-20 run on the CPU)."""
+    import numpy as np
+    from oracle import w8a8_oracle as O
+    data = np.load(ROOT / "tests" / "golden" / "w8a8_small.npz")
+    w = torch.from_numpy(O.from_bf16_bits(data["wq.w"])).to(torch.bfloat16)
+    src = nn.Linear(w.shape[1], w.shape[0], bias=False).to(torch.bfloat16)
+    with torch.no_grad():
+        src.weight.copy_(w)
+    layer = Int8Linear(src, gemm="torch")
+    np.testing.assert_array_equal(layer.weight_int8.t().contiguous().numpy(), data["wq.q"])
+    np.testing.assert_array_equal(layer.weight_scale.t().contiguous().numpy(), data["wq.s"])
+    assert layer.weight_int8.stride() == (1, w.shape[1]) and layer.weight.dtype == torch.bfloat16
 
 
 class _Attn(nn.Module):
