@@ -1,6 +1,6 @@
 // INT8 GEMM with int32 accumulation and a fused bf16 epilogue on sm_100a.
 //
-// Tensor-core path (K10 of the reference, model/int8_gemm.py:117-150, rebuilt
+// Tensor-core path (K10 of the reference, model/int8_gemm.py:13-46, rebuilt
 // for Blackwell rather than translated):
 //   * persistent kernel, one CTA per SM, grouped-M tile raster;
 //   * 128x256 output tiles, K staged 128 bytes at a time through a 4-deep
@@ -83,7 +83,7 @@ struct EpiArgs {
 
 // ------------------------------------------------------------ epilogue math
 __device__ __forceinline__ float dequant(int32_t acc, float rs, float cs) {
-  // (float(acc) * row_scale) * col_scale   (model/int8_gemm.py:145-146,193)
+  // (float(acc) * row_scale) * col_scale   (model/int8_gemm.py:41-42,89)
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), rs), cs);
 }
 

@@ -29,7 +29,7 @@ TILE = (128, 256, 128, 6, 4, 8)
 
 
 def _contract(a: torch.Tensor, b: torch.Tensor) -> None:
-    # model/int8_gemm.py:201-202
+    # model/int8_gemm.py:97-98
     if a.dtype != torch.int8 or b.dtype != torch.int8 or not a.is_contiguous() or a.shape[1] != b.shape[0]:
         raise ValueError("INT8 GEMM requires contiguous row-major activations and compatible INT8 weights")
     if a.device.type != "cuda" or b.device != a.device:
@@ -87,7 +87,7 @@ def _launch(a, b, row_scale, column_scale, bias, epilogue, residual=None, table=
 def int8_matmul(a, b, row_scale, column_scale, bias=None, *, tile=None):
     """bf16((a @ b) * row_scale * column_scale + bias) with exact int32 accumulation.
 
-    Replaces model/int8_gemm.py:200-267. a: int8 [M, K] contiguous; b: int8
+    Replaces model/int8_gemm.py:96-163. a: int8 [M, K] contiguous; b: int8
     [K, N] with any strides (the reference's weights are the [K, N] view of a
     row-major [N, K] matrix); row_scale [M, 1]; column_scale [1, N]; bias bf16
     [N] or None. ``tile`` is accepted for signature compatibility; the sm_100a
@@ -130,7 +130,7 @@ def int8_matmul_s32(a, b):
 
 
 def _torch_matmul(a, b, row_scale, column_scale, bias):
-    """The reference's cuBLASLt path (model/int8_gemm.py:188-196), kept as the
+    """The reference's cuBLASLt path (model/int8_gemm.py:84-92), kept as the
     integer known-answer comparator of ``int8_matmul``; never used as a fallback."""
     rows = a.shape[0]
     pad = max(32, -(-rows // 8) * 8) - rows

@@ -14,10 +14,10 @@ from . import _lib
 
 
 def matmul(a, b, sa, sb, bias=None, tile=(128, 256, 128, 8, 3)):
-    """bf16((a @ b) * sa * sb + bias); model/int8_tma.py:299-308.
+    """bf16((a @ b) * sa * sb + bias); model/int8_tma.py:32-41.
 
     Requires row-major int8 activations and the transposed row-major weight view
-    (``b.stride() == (1, K)``), else ValueError (model/int8_tma.py:301-302).
+    (``b.stride() == (1, K)``), else ValueError (model/int8_tma.py:34-35).
     """
     m, k = a.shape
     if a.dtype != torch.int8 or b.dtype != torch.int8 or not a.is_contiguous() or b.stride() != (1, k):

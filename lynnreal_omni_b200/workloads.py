@@ -97,7 +97,7 @@ def config1(seed: int = 0, m: int = BLOCK_TOKENS, d: int = HIDDEN, device=None) 
 
 def gemm_operands(m: int, k: int, n: int, seed: int = 219, device=None, bias: bool = False):
     """Operands in the style of the reference's install-time GEMM check
-    (script/precompile.py:382-385): int8 A [m, k], B = [n, k] int8 transposed to
+    (script/precompile.py:56-59): int8 A [m, k], B = [n, k] int8 transposed to
     a [k, n] view, row scales rand/127 [m, 1], column scales rand/127 [1, n]."""
     g = generator(seed) if device is None else generator(seed, device)
     dev = g.device

@@ -94,7 +94,7 @@ def quantize_rows(x):
 
 
 def int8_gemm_s32(a: np.ndarray, b_kn: np.ndarray) -> np.ndarray:
-    """Exact int32 accumulators acc = a @ b (model/int8_gemm.py:192; model/int8.py:51)."""
+    """Exact int32 accumulators acc = a @ b (model/int8_gemm.py:88; model/int8.py:51)."""
     at = torch.from_numpy(np.ascontiguousarray(a, dtype=np.int8))
     bt = torch.from_numpy(np.ascontiguousarray(b_kn, dtype=np.int8))
     return torch._int_mm(at, bt).numpy()
@@ -103,7 +103,7 @@ def int8_gemm_s32(a: np.ndarray, b_kn: np.ndarray) -> np.ndarray:
 def int8_epilogue(acc, row_scale, col_scale, bias=None) -> np.ndarray:
     """bf16((float(acc) * row_scale) * col_scale + bias) as float32.
 
-    model/kernels.py:27-38 (``_int8_epilogue_kernel``), model/int8_gemm.py:188-196
+    model/kernels.py:27-38 (``_int8_epilogue_kernel``), model/int8_gemm.py:84-92
     (``_torch_matmul``), model/int8.py:55-58.
     """
     out = np.asarray(acc).astype(F32) * np.asarray(row_scale, F32).reshape(-1, 1)
@@ -114,7 +114,7 @@ def int8_epilogue(acc, row_scale, col_scale, bias=None) -> np.ndarray:
 
 
 def int8_matmul(a, b_kn, row_scale, col_scale, bias=None) -> np.ndarray:
-    """INT8 GEMM with the fused bf16 epilogue (model/int8_gemm.py:117-150, 188-196)."""
+    """INT8 GEMM with the fused bf16 epilogue (model/int8_gemm.py:13-46, 84-92)."""
     return int8_epilogue(int8_gemm_s32(a, b_kn), row_scale, col_scale, bias)
 
 

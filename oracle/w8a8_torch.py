@@ -32,7 +32,7 @@ def quantize_rows(x: torch.Tensor):
 
 
 def int8_matmul(a: torch.Tensor, b_kn: torch.Tensor, row_scale, col_scale, bias=None) -> torch.Tensor:
-    """Exact int32 GEMM + bf16 epilogue (model/int8_gemm.py:188-196) -> float32 (bf16 values)."""
+    """Exact int32 GEMM + bf16 epilogue (model/int8_gemm.py:84-92) -> float32 (bf16 values)."""
     acc = torch._int_mm(a.contiguous(), b_kn)
     out = acc.to(F32) * row_scale.reshape(-1, 1).to(F32) * col_scale.reshape(1, -1).to(F32)
     if bias is not None:

@@ -6,7 +6,7 @@ Usage (needs the reference source tree, which the GPU box does not have):
 
 What runs, all on the CPU:
   * the reference's torch path: ``Int8Linear`` (model/int8.py), ``_torch_matmul``
-    (model/int8_gemm.py:188-196) and ``quantize_transformer`` (model/int8.py:71-104);
+    (model/int8_gemm.py:84-92) and ``quantize_transformer`` (model/int8.py:71-104);
   * the reference's Triton kernels (model/kernels.py) under the Triton
     interpreter (TRITON_INTERPRET=1), with two substitutions that give the
     interpreter the GPU's semantics:
@@ -141,7 +141,7 @@ def main(reference_root: str) -> None:
     out["wq.q"] = layer.weight_int8.t().contiguous().numpy()
     out["wq.s"] = layer.weight_scale.t().contiguous().numpy()
 
-    # ---- _torch_matmul, the reference's integer KAT (script/precompile.py:381-390)
+    # ---- _torch_matmul, the reference's integer KAT (script/precompile.py:55-62)
     for name, (m, k, n, with_bias) in {"mm_a": (1, 64, 48, False), "mm_b": (7, 96, 40, True),
                                        "mm_c": (33, 256, 264, False), "mm_d": (130, 256, 136, True)}.items():
         a, b, rs, cs, bb = workloads.gemm_operands(m, k, n, seed=1000 + m, bias=with_bias)

@@ -181,8 +181,8 @@ def test_rms_kernels_vs_reference_golden(g, name):
 
 
 def test_residual_fusion_equals_separate_kernels():
-    """Known-answer check of the reference (script/precompile.py:393-403,
-    model/acceleration.py:279-286): the fused residual+norm+quant equals the
+    """Known-answer check of the reference (script/precompile.py:65-77,
+    model/acceleration.py:31-38): the fused residual+norm+quant equals the
     separate gated residual followed by the norm+quant, bit for bit."""
     gen = torch.Generator().manual_seed(219)
     x = torch.randn(1, 32, 5376, generator=gen).to(torch.bfloat16).to(DEV)
