@@ -51,13 +51,24 @@ def parse_args():
                    help="block: token rows of the latent, sharded over the GPUs; flash: token rows per GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels"], default="block",
+    p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels", "kernel"],
+                   default="block",
                    help="block: config 2 per GPU (weak scaling); stack: config 4, 42 blocks x 3 denoiser "
                         "steps on 64512 tokens sharded over the GPUs with a final all-gather; sweep: "
                         "config 3 GEMM shapes, row-sharded, TOP/s per shape beside cuBLASLt; flash: one "
                         "block at the released Flash shapes through the fused-block caller, attention included; "
                         "reference_kernels: each kernel beside the reference's compiled GPU kernel (installed in "
-                        "baseline/_ref) on the same inputs, device time and output identity")
+                        "baseline/_ref) on the same inputs, device time and output identity; kernel: one kernel "
+                        "(--case) on synthetic inputs, for profilers and timing")
+    p.add_argument("--case", default="rms",
+                   choices=["gemm", "rms", "quant", "gated", "residual_rms", "qk", "compress", "restore",
+                            "restore_torch", "layout", "attn", "attn_sdpa"], help="kernel workload: which kernel")
+    p.add_argument("--m", type=int, default=12240, help="kernel workload: rows / tokens")
+    p.add_argument("--k", type=int, default=6144, help="kernel workload: GEMM depth")
+    p.add_argument("--n", type=int, default=24576, help="kernel workload: GEMM width")
+    p.add_argument("--d", type=int, default=6144, help="kernel workload: hidden size")
+    p.add_argument("--epi", choices=["none", "gelu", "gated"], default="none", help="kernel workload: GEMM epilogue")
+    p.add_argument("--graph", action="store_true", help="kernel workload: time a CUDA-graph replay of the launches")
     p.add_argument("--layers", type=int, default=42)
     p.add_argument("--stack-tokens", type=int, default=64512)
     p.add_argument("--compress", action="store_true",
@@ -993,6 +1004,138 @@ def run_reference_kernels(args, rank, world, local):
                       "reference": f"baseline/_ref, Triton {triton.__version__}", "ops": rows}))
 
 
+def _case_time(fn, iters: int, warmup: int, graph: bool = False):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if graph:
+        # capture `iters` calls once and time one replay: device time without
+        # the host-side cost of issuing each call
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
+        reps = 1
+    else:
+        run = fn
+        reps = iters
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def run_kernel_case(args):
+    """One kernel of the path on synthetic inputs, for profilers and timing:
+    ``--case`` gemm (``--epi`` none/gelu/gated), rms (K4), quant (K1), gated
+    (K5), residual_rms (K8), qk (Q/K RMSNorm + RoPE), compress / restore /
+    restore_torch / layout (token compression on a 21 x 48 x 64 grid), attn /
+    attn_sdpa (48 heads x 128 at ``--m`` tokens). Launches the kernel
+    ``--steps`` times on cuda:0 after ``--warmup`` calls (``--graph``: as one
+    CUDA-graph replay) and prints the mean CUDA-event time per launch and the
+    algorithmic rate."""
+    from types import SimpleNamespace
+    from lynnreal_omni_b200 import _lib
+    _lib.load()
+    a = args
+    from lynnreal_omni_b200 import kernels as K
+    from lynnreal_omni_b200.int8_gemm import int8_matmul, int8_matmul_gated_residual, int8_matmul_gelu
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {"case": a.case, "graph": a.graph}
+    if a.case == "gemm":
+        A = torch.randint(-127, 128, (a.m, a.k), device=dev, dtype=torch.int8, generator=g)
+        B = torch.randint(-127, 128, (a.n, a.k), device=dev, dtype=torch.int8, generator=g).t()
+        rs = torch.rand(a.m, 1, device=dev, generator=g) / 127
+        cs = torch.rand(1, a.n, device=dev, generator=g) / 127
+        bias = (0.02 * torch.randn(a.n, device=dev, generator=g)).to(torch.bfloat16)
+        if a.epi == "gelu":
+            fn = lambda: int8_matmul_gelu(A, B, rs, cs, bias)  # noqa: E731
+        elif a.epi == "gated":
+            res = torch.randn(1, a.m, a.n, device=dev, generator=g).to(torch.bfloat16)
+            table = (0.1 * torch.randn(1, 6 * a.n, device=dev, generator=g)).to(torch.bfloat16)
+            idx = torch.zeros(a.m, dtype=torch.int64, device=dev)
+            fn = lambda: int8_matmul_gated_residual(A, B, rs, cs, bias, res, table, idx, 5)  # noqa: E731
+        else:
+            fn = lambda: int8_matmul(A, B, rs, cs, bias)  # noqa: E731
+        ms = _case_time(fn, a.steps, a.warmup, a.graph)
+        out.update(m=a.m, k=a.k, n=a.n, epi=a.epi, ms=ms, tops=2.0 * a.m * a.n * a.k / (ms / 1e3) / 1e12,
+                   algorithmic_bytes=a.m * a.k + a.n * a.k + 2 * a.m * a.n + 4 * a.m + 6 * a.n)
+    elif a.case == "qk":
+        heads, hd = a.d // 128, 128
+        qkv = torch.randn(1, a.m, 3 * a.d, device=dev, generator=g).to(torch.bfloat16)
+        q, k, _ = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+        nq = SimpleNamespace(weight=torch.ones(hd, device=dev, dtype=torch.bfloat16), eps=1e-6)
+        phase = torch.randn(a.m, hd, device=dev, generator=g)
+        rot = (phase.cos(), phase.sin())
+        ms = _case_time(lambda: K.qk_norm_rope(q, k, nq, nq, rot), a.steps, a.warmup, a.graph)
+        nbytes = 8 * a.m * a.d + 8 * a.m * hd + 4 * hd
+        out.update(m=a.m, d=a.d, heads=heads, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    elif a.case in ("attn", "attn_sdpa"):
+        from lynnreal_omni_b200.attention import attention_bshd
+        heads = a.d // 128
+        qkv = torch.randn(1, a.m, 3 * a.d, device=dev, generator=g).to(torch.bfloat16)
+        q, k, v = [t.unflatten(-1, (heads, -1)) for t in qkv.chunk(3, dim=-1)]
+        if a.case == "attn":
+            fn = lambda: attention_bshd(q, k, v)  # noqa: E731
+        else:
+            qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+            fn = lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)  # noqa: E731
+        ms = _case_time(fn, a.steps, a.warmup, a.graph)
+        flops = 4.0 * heads * a.m * a.m * 128
+        out.update(m=a.m, heads=heads, ms=ms, tflops=flops / (ms / 1e3) / 1e12)
+    elif a.case in ("compress", "restore", "restore_torch", "layout"):
+        from lynnreal_omni_b200 import flash
+        t, h, w = torch.meshgrid(torch.arange(21), torch.arange(48), torch.arange(64), indexing="ij")
+        pos = torch.stack([t, h, w], -1).reshape(-1, 3).to(dev)
+        tags = torch.zeros(pos.shape[0], dtype=torch.int64, device=dev)
+        keep, inverse = flash.spatial_layout(pos, tags)
+        s, kept = pos.shape[0], keep.numel()
+        if a.case == "layout":
+            ms = _case_time(lambda: flash.spatial_layout(pos, tags), a.steps, a.warmup, False)
+            out.update(rows=s, kept=kept, ms=ms)
+        else:
+            full = torch.randn(1, s, a.d, device=dev, generator=g).to(torch.bfloat16)
+            if a.case == "compress":
+                fn = lambda: flash.index_select(full, 1, keep)  # noqa: E731
+                nbytes = 4 * kept * a.d + 8 * kept
+            else:
+                comp = torch.randn(1, kept, a.d, device=dev, generator=g).to(torch.bfloat16)
+                inp = torch.randn(1, kept, a.d, device=dev, generator=g).to(torch.bfloat16)
+                if a.case == "restore":
+                    fn = lambda: flash.restore(full, comp, inp, inverse, 1.0)  # noqa: E731
+                else:
+                    fn = lambda: full + ((comp - inp) * 1.0).index_select(1, inverse)  # noqa: E731
+                nbytes = 4 * s * a.d + 4 * kept * a.d + 8 * s
+            ms = _case_time(fn, a.steps, a.warmup, a.graph)
+            out.update(rows=s, kept=kept, d=a.d, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    else:
+        x = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.randn(1, a.m, a.d, device=dev, generator=g).to(torch.bfloat16)
+        table = (0.1 * torch.randn(1, 6 * a.d, device=dev, generator=g)).to(torch.bfloat16)
+        idx = torch.zeros(a.m, dtype=torch.int64, device=dev)
+        norm = SimpleNamespace(weight=(1 + 0.05 * torch.randn(a.d, device=dev, generator=g)).to(torch.bfloat16),
+                               eps=1e-6)
+        if a.case == "rms":
+            fn, per_elem = (lambda: K._rms_adaln_quant_int8(x, norm, table, idx, 0, 1)), 3
+        elif a.case == "quant":
+            fn, per_elem = (lambda: K.quantize_rows(x.view(a.m, a.d))), 3
+        elif a.case == "gated":
+            fn, per_elem = (lambda: K._gated_residual(x, y, table, idx, 2)), 6
+        else:
+            fn, per_elem = (lambda: K.residual_rms_quant(x, y, norm, table, idx)), 7
+        ms = _case_time(fn, a.steps, a.warmup, a.graph)
+        nbytes = per_elem * a.m * a.d + 4 * a.m
+        out.update(m=a.m, d=a.d, ms=ms, algorithmic_bytes=nbytes, gbs=nbytes / (ms / 1e3) / 1e9)
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
@@ -1008,6 +1151,8 @@ def main():
         run_flash(args, rank, world, local)
     elif args.workload == "reference_kernels":
         run_reference_kernels(args, rank, world, local)
+    elif args.workload == "kernel":
+        run_kernel_case(args)
     else:
         run_ours(args, rank, world, local)
 
