@@ -3,7 +3,7 @@
 // Arithmetic contract (what "bit-exact" means for these kernels):
 //   * every fp32 product and sum is rounded on its own (no FMA contraction),
 //     matching the reference's `enable_fp_fusion=False` launches
-//     (model/kernels.py:270,287,302; model/int8_gemm.py:243,260);
+//     (model/kernels.py:270,287,302; model/int8_gemm.py:139,156);
 //   * bf16 rounding points are round-to-nearest-even;
 //   * divisions and the RMS reciprocal square root either as the reference's
 //     compiled kernels execute them on the GPU (div.full, rsqrt.approx) or
@@ -78,11 +78,32 @@ __device__ __forceinline__ float bamax_final(uint32_t acc) { return fmaxf(bf_lo(
 
 constexpr uint32_t kBf2One = 0x3f803f80u;  // (1.0, 1.0) in bf16x2
 
+// Widen both bf16 halves of a word to fp32. With LR_WIDEN_FMA the widening is
+// the mixed-precision add.rn.f32.bf16 of each half and -0.0 (exact for every
+// value, signed zeros included), an FMA-pipe instruction, instead of a shift
+// and a mask on the integer pipe.
+#ifndef LR_WIDEN_FMA
+#define LR_WIDEN_FMA 1
+#endif
+__device__ __forceinline__ float2 widen2(uint32_t w) {
+#if LR_WIDEN_FMA
+  float2 f;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "add.rn.f32.bf16 %0, l, 0f80000000;\n\tadd.rn.f32.bf16 %1, h, 0f80000000;\n\t}"
+      : "=f"(f.x), "=f"(f.y)
+      : "r"(w));
+  return f;
+#else
+  return make_float2(bf_lo(w), bf_hi(w));
+#endif
+}
+
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-  f[0] = bf_lo(v.x); f[1] = bf_hi(v.x);
-  f[2] = bf_lo(v.y); f[3] = bf_hi(v.y);
-  f[4] = bf_lo(v.z); f[5] = bf_hi(v.z);
-  f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
+  const float2 a = widen2(v.x), b = widen2(v.y), c = widen2(v.z), d = widen2(v.w);
+  f[0] = a.x; f[1] = a.y;
+  f[2] = b.x; f[3] = b.y;
+  f[4] = c.x; f[5] = c.y;
+  f[6] = d.x; f[7] = d.y;
 }
 // Round eight fp32 values to bf16 and pack them.
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {

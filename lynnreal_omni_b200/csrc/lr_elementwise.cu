@@ -104,9 +104,14 @@ __global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : LR_QUA
                                                                   int64_t row_stride, int width,
                                                                   int8_t* __restrict__ q,
                                                                   float* __restrict__ scales,
-                                                                  int64_t rows) {
+                                                                  int64_t rows, int arith) {
   __shared__ float red[kWarps];
   int64_t row = blockIdx.x;
+  // arith < 0: the device's mode (lr_set_arithmetic); LR_ARITH_TORCH_CUDA: the
+  // scale is absmax times the float reciprocal of 127 (how PyTorch divides a
+  // CUDA tensor by a scalar), the quotient IEEE
+  const bool gpu = arith < 0 ? arith_gpu() : arith == LR_ARITH_REFERENCE_GPU;
+  const bool by_reciprocal = arith == LR_ARITH_TORCH_CUDA;
   if (row >= rows) return;
   uint4 raw[C];
   load_row<C, VEC, true>(raw, x + row * row_stride, width);
@@ -119,8 +124,8 @@ __global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : LR_QUA
 #pragma unroll
     for (int c = 0; c < C; ++c) amax2 = bamax8(amax2, raw[c]);
     const float amax = block_max<kWarps>(bamax_final(amax2), red);
-    const bool gpu = arith_gpu();
-    const float s = row_scale_from_absmax(amax, gpu);
+    const float s = by_reciprocal ? __fmul_rn(fmaxf(amax, 1.0e-8f), 1.0f / 127.0f)
+                                  : row_scale_from_absmax(amax, gpu);
     const float inv = __frcp_rn(s);
     int8_t* dst = q + row * (int64_t)width;
 #pragma unroll
@@ -152,15 +157,35 @@ __global__ void __launch_bounds__(kThreads, (C > 4 ? LR_QUANT_WIDE_MINB : LR_QUA
 // chains go through `stage` to the thread with their index, so block_sum then
 // reduces them in the reference's butterflies. Squares of bf16 values are
 // exact in fp32, so each fused multiply-add equals the separate multiply and add.
+// Running max of magnitudes over packed bf16 values: max.xorsign.abs keeps
+// max(|acc|, |a|) per lane (the sign bit it sets is discarded at the end).
+__device__ __forceinline__ uint32_t bmaxabs2(uint32_t acc, uint32_t a) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(a));
+  return d;
+}
+__device__ __forceinline__ float bmaxabs_final(uint32_t acc) { return fmaxf(fabsf(bf_lo(acc)), fabsf(bf_hi(acc))); }
+
+// acc + lo(u)^2, then + hi(u)^2: the mixed-precision fma.rn.f32.bf16 of
+// sm_100 multiplies the bf16 halves exactly and rounds the sum once, as the
+// fp32 fma of the widened values does, without unpacking them first.
+__device__ __forceinline__ float sumsq_word(float acc, uint32_t u) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\t"
+      "fma.rn.f32.bf16 %0, l, l, %0;\n\tfma.rn.f32.bf16 %0, h, h, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(u));
+  return acc;
+}
+
 template <int C>
 __device__ __forceinline__ float sumsq_part8(const uint4 (&v)[C]) {
   float part = 0.0f;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    float f[8];
-    unpack8(v[c], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) part = __fmaf_rn(f[e], f[e], part);
+    part = sumsq_word(part, v[c].x);
+    part = sumsq_word(part, v[c].y);
+    part = sumsq_word(part, v[c].z);
+    part = sumsq_word(part, v[c].w);
   }
   return part;
 }
@@ -322,6 +347,178 @@ __global__ void __launch_bounds__(kThreads, (C <= 4 ? LR_RMS_MINB : 0)) rms_mod_
     }
     row = next;
   }
+}
+
+// ------------------------------------------------- K4/K8 in the 16-column layout
+// The int8-output RMSNorm kernels of the reference lay a row out over 256
+// threads with 16 columns each: reference thread t' sums the squares of
+// columns 4096 r + 16 t' + [0, 16), r = 0, 1, ..., in order, then the row sum
+// is an xor butterfly inside each of its 8 warps and across the warps. Here a
+// 128-thread CTA owns a row and thread t stands in for reference threads t
+// and t + 128 (reference warps g and g + 4 of warp g), so every chain lives in
+// one thread: no lane-pair shuffles and no transpose through shared memory.
+// Group k of a thread is (t' = t + 128 (k / R), r = k % R); each group is one
+// 32-byte load (sm_100 256-bit vector access), a warp reads 1 KB contiguous.
+// The first cross-warp step of the reference's butterfly (w + 4 into w) is the
+// sum of a thread's two chains' warp sums; the last two go through shared
+// memory. Results are identical to rms_mod_kernel. Rows of 2048 to 8192
+// columns, a multiple of 16.
+constexpr int kQ16Threads = 128;
+
+struct Bf16x16 {
+  uint32_t w[8];
+};
+
+__device__ __forceinline__ Bf16x16 ld256_stream(const void* p) {
+  Bf16x16 v;
+  asm volatile("ld.global.cs.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ Bf16x16 ld256_keep(const void* p) {
+  Bf16x16 v;
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st256(void* p, const Bf16x16& v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+               "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+               : "memory");
+}
+__device__ __forceinline__ Bf16x16 splat16(uint32_t w) {
+  Bf16x16 v;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v.w[i] = w;
+  return v;
+}
+
+// The per-row work of the 16-column K4/K8 kernels, from the row's groups in
+// registers: residual (K8), sums of squares, RMS factor, normalise +
+// modulate, absmax, quantise, stores. Two block barriers; every thread of the
+// CTA calls it for the same row.
+template <int NG, int R, bool RESID, bool MOD>
+__device__ __forceinline__ void q16_row(const RmsArgs& a, int64_t row, const int (&col)[NG], const bool (&ok)[NG],
+                                        Bf16x16 (&v)[NG], const Bf16x16 (&d)[RESID ? NG : 1], float* red_sum,
+                                        float* red_max, const bf16* trow) {
+  const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
+  const int hidden = a.hidden;
+  const bool have_table = trow != nullptr;
+  if (RESID) {
+    // v = bf16(x + bf16(gate * update))   (model/kernels.py:101-105)
+    const uint32_t gate_default = a.table == nullptr ? kBf2One : 0u;
+#pragma unroll
+    for (int k = 0; k < NG; ++k) {
+      if (!ok[k]) continue;
+      const Bf16x16 g = have_table ? ld256_keep(trow + (int64_t)a.gate_slot * hidden + col[k]) : splat16(gate_default);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k].w[i] = badd2(v[k].w[i], bmul2(g.w[i], d[RESID ? k : 0].w[i]));
+      st256(a.residual_out + row * (int64_t)hidden + col[k], v[k]);
+    }
+  }
+  // chains: .x over the groups of t' = t, .y over those of t' = t + 128
+  // (columns past the row are zeros and add exactly nothing)
+  float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int k = 0; k < NG; ++k) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (k < R) acc.x = sumsq_word(acc.x, v[k].w[i]);
+      else acc.y = sumsq_word(acc.y, v[k].w[i]);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    acc.x = __fadd_rn(acc.x, __shfl_xor_sync(0xffffffffu, acc.x, off));
+    acc.y = __fadd_rn(acc.y, __shfl_xor_sync(0xffffffffu, acc.y, off));
+  }
+  if (lane == 0) red_sum[warp] = __fadd_rn(acc.x, acc.y);  // s[w] + s[w + 4]
+  __syncthreads();
+  const float ss = __fadd_rn(__fadd_rn(red_sum[0], red_sum[2]), __fadd_rn(red_sum[1], red_sum[3]));
+  const bool gpu = arith_gpu();
+  // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65,106)
+  const float rs = rms_factor(ss, (float)hidden, a.eps, gpu);
+  const float2 r2 = make_float2(rs, rs);
+  uint32_t amax2 = 0u;
+#pragma unroll
+  for (int k = 0; k < NG; ++k) {
+    if (!ok[k]) continue;
+    const Bf16x16 w = ld256_keep(a.weight + col[k]);
+    // n = bf16((x * r) * w)   (model/kernels.py:65-68,106-108)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 n = __fmul2_rn(__fmul2_rn(widen2(v[k].w[i]), r2), widen2(w.w[i]));
+      v[k].w[i] = cvt2(n.x, n.y);
+    }
+    if (MOD && have_table) {
+      // m = bf16(bf16(n * bf16(1 + scale)) + shift)   (model/kernels.py:117-120)
+      const Bf16x16 sc = ld256_keep(trow + (int64_t)a.scale_slot * hidden + col[k]);
+      const Bf16x16 sh = ld256_keep(trow + (int64_t)a.shift_slot * hidden + col[k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k].w[i] = badd2(bmul2(v[k].w[i], badd2(kBf2One, sc.w[i])), sh.w[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax2 = bmaxabs2(amax2, v[k].w[i]);
+  }
+  float amax = bmaxabs_final(amax2);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if (lane == 0) red_max[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(red_max[0], red_max[1]), fmaxf(red_max[2], red_max[3]));
+  const float s = row_scale_from_absmax(amax, gpu);
+  const float inv = __frcp_rn(s);
+  int8_t* dst = a.q + row * (int64_t)hidden;
+#pragma unroll
+  for (int k = 0; k < NG; ++k) {
+    if (!ok[k]) continue;
+    const uint2 lo = quant8(make_uint4(v[k].w[0], v[k].w[1], v[k].w[2], v[k].w[3]), s, inv, gpu);
+    const uint2 hi = quant8(make_uint4(v[k].w[4], v[k].w[5], v[k].w[6], v[k].w[7]), s, inv, gpu);
+    *reinterpret_cast<uint4*>(dst + col[k]) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+  }
+  if (t == 0) a.scales[row] = s;
+}
+
+template <int NG, int R>
+__device__ __forceinline__ void q16_columns(int (&col)[NG], bool (&ok)[NG], int hidden) {
+#pragma unroll
+  for (int k = 0; k < NG; ++k) {
+    col[k] = 4096 * (k % R) + 16 * ((int)threadIdx.x + kQ16Threads * (k / R));
+    ok[k] = col[k] < hidden;
+  }
+}
+
+// One row per CTA of the same layout, for a grid of all rows: rows in flight
+// are CTAs, not registers (a persistent form that prefetched the next row in
+// registers held 4 CTAs per SM and ran 74 us at 12240 x 6144; staging the next
+// rows, or the weights and modulation, in shared memory by cp.async was
+// slower still).
+#ifndef LR_Q16R_MINB
+#define LR_Q16R_MINB 8
+#endif
+template <int NG, int R, bool RESID, bool MOD>
+__global__ void __launch_bounds__(kQ16Threads, LR_Q16R_MINB) rms_quant16_row_kernel(const RmsArgs a) {
+  __shared__ float red_sum[kQ16Threads / 32];
+  __shared__ float red_max[kQ16Threads / 32];
+  const int64_t row = blockIdx.x;
+  int col[NG];
+  bool ok[NG];
+  q16_columns<NG, R>(col, ok, a.hidden);
+  Bf16x16 v[NG], d[RESID ? NG : 1];
+#pragma unroll
+  for (int k = 0; k < NG; ++k) {
+    v[k] = ok[k] ? ld256_stream(a.x + row * (int64_t)a.hidden + col[k]) : splat16(0u);
+    if (RESID) d[RESID ? k : 0] = ok[k] ? ld256_stream(a.update + row * (int64_t)a.hidden + col[k]) : splat16(0u);
+  }
+  bool bad;
+  const bf16* trow = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence, row, bad);
+  if (bad && threadIdx.x == 0) flag_error(kDevErrTableIndex);
+  q16_row<NG, R, RESID, MOD>(a, row, col, ok, v, d, red_sum, red_max, trow);
 }
 
 // Two rows per CTA: both rows' partial sums (and then absmaxes) go through one
@@ -865,7 +1062,8 @@ constexpr int64_t kMaxRows = 0x7fffffff;
 // Grid of a persistent row kernel: every CTA that fits at once on the GPU
 // (occupancy of this instantiation x SM count), capped by the row count.
 template <typename Kernel>
-unsigned persistent_grid(Kernel kernel, int64_t rows, bool persistent = true) {
+unsigned persistent_grid(Kernel kernel, int64_t rows, bool persistent = true, int threads = kThreads,
+                         size_t smem = 0) {
   if (!persistent) return (unsigned)rows;  // one row per CTA
   static std::mutex mu;
   static std::unordered_map<const void*, int> per_sm;
@@ -876,7 +1074,7 @@ unsigned persistent_grid(Kernel kernel, int64_t rows, bool persistent = true) {
     if (it != per_sm.end()) {
       n = it->second;
     } else {
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, 0) != cudaSuccess || n < 1) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
         cudaGetLastError();
         n = 1;
       }
@@ -922,8 +1120,8 @@ extern "C" int lr_get_arithmetic(int* mode) {
   return LR_OK;
 }
 
-extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
-                                int8_t* q, float* scales, void* stream) {
+static int quantize_rows_launch(const void* x, int64_t rows, int64_t width, int64_t row_stride, int8_t* q,
+                                float* scales, int arith, void* stream) {
   LR_REQUIRE(rows >= 0 && width > 0, "quantize_rows: invalid shape [%lld, %lld]", (long long)rows,
              (long long)width);
   LR_REQUIRE(row_stride >= width, "quantize_rows: row stride %lld < width %lld",
@@ -938,11 +1136,23 @@ extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int6
   const bf16* xp = static_cast<const bf16*>(x);
   LR_CHUNK_DISPATCH(C, {
     if (vec)
-      lr::quantize_rows_kernel<kC, true><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows);
+      lr::quantize_rows_kernel<kC, true><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, true>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows, arith);
     else
-      lr::quantize_rows_kernel<kC, false><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows);
+      lr::quantize_rows_kernel<kC, false><<<lr::persistent_grid(lr::quantize_rows_kernel<kC, false>, rows, lr::Prefetch<kC>::kOn), lr::kThreads, 0, s>>>(xp, row_stride, (int)width, q, scales, rows, arith);
   });
   return lr::launch_status("quantize_rows");
+}
+
+extern "C" int lr_quantize_rows(const void* x, int64_t rows, int64_t width, int64_t row_stride,
+                                int8_t* q, float* scales, void* stream) {
+  return quantize_rows_launch(x, rows, width, row_stride, q, scales, -1, stream);
+}
+
+extern "C" int lr_quantize_rows_arith(const void* x, int64_t rows, int64_t width, int64_t row_stride,
+                                      int8_t* q, float* scales, int arithmetic, void* stream) {
+  LR_REQUIRE(arithmetic == LR_ARITH_IEEE || arithmetic == LR_ARITH_REFERENCE_GPU ||
+             arithmetic == LR_ARITH_TORCH_CUDA, "quantize_rows: unknown arithmetic %d", arithmetic);
+  return quantize_rows_launch(x, rows, width, row_stride, q, scales, arithmetic, stream);
 }
 
 extern "C" int lr_int8_epilogue(const int32_t* acc, int64_t rows, int64_t cols,
@@ -1002,8 +1212,42 @@ bool vec_ok(int64_t hidden, std::initializer_list<const void*> ptrs) {
 #define LR_RMS2_OFF 0  // 1: the residual variant runs the one-row kernel too (tuning knob)
 #endif
 
+#ifndef LR_Q16_OFF
+#define LR_Q16_OFF 0  // 1: K4/K8 run the 8-column-chunk kernels (tuning knob)
+#endif
+// K4/K8 in the reference's 16-column layout (rms_quant16_row_kernel): rows of
+// 2048 to 8192 columns, a multiple of 16, with 32-byte aligned bf16 operands
+// and 16-byte aligned int8 rows.
+static bool q16_ok(const lr::RmsArgs& a) {
+  if (LR_Q16_OFF || a.hidden < 2048 || a.hidden > 8192 || a.hidden % 16) return false;
+  for (const void* p : {(const void*)a.x, (const void*)a.update, (const void*)a.weight, (const void*)a.table,
+                        (const void*)a.residual_out})
+    if (p && !lr::aligned(p, 32)) return false;
+  return lr::aligned(a.q, 16) && (a.table == nullptr || a.table_width % 16 == 0);
+}
+
+template <int NG, int R, bool RESID, bool MOD>
+static void q16_row_launch(const lr::RmsArgs& a, int64_t rows, cudaStream_t s) {
+  lr::rms_quant16_row_kernel<NG, R, RESID, MOD><<<(unsigned)rows, lr::kQ16Threads, 0, s>>>(a);
+}
+
+template <int NG, int R>
+static void q16_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, cudaStream_t s) {
+  if (resid) {
+    if (mod) q16_row_launch<NG, R, true, true>(a, rows, s); else q16_row_launch<NG, R, true, false>(a, rows, s);
+  } else {
+    if (mod) q16_row_launch<NG, R, false, true>(a, rows, s); else q16_row_launch<NG, R, false, false>(a, rows, s);
+  }
+}
+
 static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, bool quant, bool vec,
                       cudaStream_t s) {
+  if (quant && q16_ok(a)) {
+    if (a.hidden <= 4096) q16_launch<2, 1>(a, rows, resid, mod, s);
+    else if (a.hidden <= 6144) q16_launch<3, 2>(a, rows, resid, mod, s);
+    else q16_launch<4, 2>(a, rows, resid, mod, s);
+    return lr::launch_status("rms_adaln");
+  }
   const int C = pick_chunks(a.hidden);
   if (C < 0) return lr::set_error(LR_ERR_UNSUPPORTED, "rms_adaln: hidden %d > 32768", a.hidden);
 // The residual variant (K8) of rows of up to 4 chunks per thread runs two rows
