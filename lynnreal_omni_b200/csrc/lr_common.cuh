@@ -163,22 +163,27 @@ __device__ __forceinline__ int quant_i8(float v, float s, bool gpu) {
 }
 
 // Eight bf16 values -> eight int8 (packed in a uint2), exactly
-// RNE(clamp(v / s, -127, 127)) with the IEEE quotient v / s.
+// RNE(clamp(v / s, -127, 127)) for the quotient v / s of the chosen
+// arithmetic: IEEE division, or (`gpu`) div.full.f32, which the compiled
+// reference uses.
 //   * s >= absmax/127 of the row, so |v / s| < 127.5 and the clamp never binds
-//     for finite values;
+//     for finite values (div.full.f32 is within 2 ulp of v / s);
 //   * q0 = v * (1/s) (both IEEE-rounded) lies within 2^-16 of v / s for
-//     |v / s| < 128, so it rounds to the same integer unless it is within
-//     2^-14 of a half-integer; those (rare) rows redo the IEEE division;
+//     |v / s| < 128, and so does either quotient (IEEE: exactly rounded;
+//     div.full.f32: within 2 ulp, at most 2^-16 below 128), so all three round
+//     to the same integer unless q0 is within 2^-14 of a half-integer; those
+//     (rare) chunks redo the quotient itself;
 //   * rounding to an integer is the float add of 1.5*2^23 (exact RNE for
 //     |q| < 2^22), whose low mantissa byte is the two's-complement int8.
-// With `gpu` the quotient is div.full.f32 itself, as the compiled reference
-// forms it (within 2 ulp of v / s, so the clamp still never binds).
+#ifndef LR_QUANT_FAST_GPU
+#define LR_QUANT_FAST_GPU 1  // 0: div.full.f32 on every element in the gpu arithmetic (tuning knob)
+#endif
 __device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool gpu) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   float f[8];
   unpack8(v, f);
   uint32_t b[8];
-  if (gpu) {
+  if (gpu && !LR_QUANT_FAST_GPU) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(div_full(f[e], s), kMagic));
     const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
@@ -201,7 +206,7 @@ __device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool
   }
   if (near_tie) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(__fdiv_rn(f[e], s), kMagic));
+    for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(gpu ? div_full(f[e], s) : __fdiv_rn(f[e], s), kMagic));
   }
   const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
   const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);

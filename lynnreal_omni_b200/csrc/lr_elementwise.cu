@@ -521,6 +521,81 @@ __global__ void __launch_bounds__(kQ16Threads, LR_Q16R_MINB) rms_quant16_row_ker
   q16_row<NG, R, RESID, MOD>(a, row, col, ok, v, d, red_sum, red_max, trow);
 }
 
+// --------------------------------------------------- K3 in the 8-column layout
+// The reference's bf16-output RMSNorm kernel lays a row out over 256 threads
+// with 8 columns each: reference thread t' sums the squares of columns
+// 2048 c + 8 t' + [0, 8), c = 0, 1, ..., in order, then the same butterflies
+// as the int8-output kernels. As in rms_quant16_row_kernel, a 128-thread CTA
+// owns a row and thread t stands in for reference threads t and t + 128, so
+// the chains need no exchange; chunk j of a thread is (t' = t + 128 (j % 2),
+// c = j / 2), one 16-byte access. Results are identical to rms_mod_kernel.
+#ifndef LR_K3R_MINB
+#define LR_K3R_MINB 8
+#endif
+template <int C, bool MOD>
+__global__ void __launch_bounds__(kQ16Threads, LR_K3R_MINB) rms_bf16_row_kernel(const RmsArgs a) {
+  __shared__ float red_sum[kQ16Threads / 32];
+  const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
+  const int hidden = a.hidden;
+  const int64_t row = blockIdx.x;
+  int col[2 * C];
+#pragma unroll
+  for (int j = 0; j < 2 * C; ++j) col[j] = 2048 * (j / 2) + 8 * (t + kQ16Threads * (j % 2));
+  uint4 v[2 * C];
+  const bf16* xrow = a.x + row * (int64_t)hidden;
+#pragma unroll
+  for (int j = 0; j < 2 * C; ++j) v[j] = load_chunk<true, true>(xrow, col[j], hidden);
+  bool bad;
+  const bf16* trow = table_row_ptr(a.table, a.table_rows, a.table_width, a.indices, a.sequence, row, bad);
+  if (bad && t == 0) flag_error(kDevErrTableIndex);
+  float2 acc = make_float2(0.0f, 0.0f);  // .x: t' = t, .y: t' = t + 128
+#pragma unroll
+  for (int j = 0; j < 2 * C; ++j) {
+    float& c = (j % 2) ? acc.y : acc.x;
+    c = sumsq_word(c, v[j].x);
+    c = sumsq_word(c, v[j].y);
+    c = sumsq_word(c, v[j].z);
+    c = sumsq_word(c, v[j].w);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    acc.x = __fadd_rn(acc.x, __shfl_xor_sync(0xffffffffu, acc.x, off));
+    acc.y = __fadd_rn(acc.y, __shfl_xor_sync(0xffffffffu, acc.y, off));
+  }
+  if (lane == 0) red_sum[warp] = __fadd_rn(acc.x, acc.y);  // s[w] + s[w + 4]
+  __syncthreads();
+  const float ss = __fadd_rn(__fadd_rn(red_sum[0], red_sum[2]), __fadd_rn(red_sum[1], red_sum[3]));
+  // r = 1 / sqrt(ss / hidden + eps)   (model/kernels.py:65)
+  const float rs = rms_factor(ss, (float)hidden, a.eps, arith_gpu());
+  const float2 r2 = make_float2(rs, rs);
+  bf16* orow = a.out + row * (int64_t)hidden;
+#pragma unroll
+  for (int j = 0; j < 2 * C; ++j) {
+    if (col[j] >= hidden) continue;
+    const uint4 w = load_chunk<true, false>(a.weight, col[j], hidden);
+    const uint32_t xw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t m[4];
+    // n = bf16((x * r) * w)   (model/kernels.py:65-68)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 n = __fmul2_rn(__fmul2_rn(widen2(xw[i]), r2), widen2(ww[i]));
+      m[i] = cvt2(n.x, n.y);
+    }
+    if (MOD && trow != nullptr) {
+      // out = bf16(bf16(n * bf16(1 + scale)) + shift)   (model/kernels.py:77-78)
+      const uint4 sc = load_chunk<true, false>(trow + (int64_t)a.scale_slot * hidden, col[j], hidden);
+      const uint4 sh = load_chunk<true, false>(trow + (int64_t)a.shift_slot * hidden, col[j], hidden);
+      m[0] = badd2(bmul2(m[0], badd2(kBf2One, sc.x)), sh.x);
+      m[1] = badd2(bmul2(m[1], badd2(kBf2One, sc.y)), sh.y);
+      m[2] = badd2(bmul2(m[2], badd2(kBf2One, sc.z)), sh.z);
+      m[3] = badd2(bmul2(m[3], badd2(kBf2One, sc.w)), sh.w);
+    }
+    *reinterpret_cast<uint4*>(orow + col[j]) = make_uint4(m[0], m[1], m[2], m[3]);
+  }
+}
+
 // Two rows per CTA: both rows' partial sums (and then absmaxes) go through one
 // block reduction, halving the barriers per row and giving each thread two
 // independent rows of work between them. Each row's reduction tree is exactly
@@ -1240,12 +1315,27 @@ static void q16_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod,
   }
 }
 
+#ifndef LR_K3R_OFF
+#define LR_K3R_OFF 0  // 1: K3 runs the 256-thread chunk kernel (tuning knob)
+#endif
+
 static int rms_launch(const lr::RmsArgs& a, int64_t rows, bool resid, bool mod, bool quant, bool vec,
                       cudaStream_t s) {
   if (quant && q16_ok(a)) {
     if (a.hidden <= 4096) q16_launch<2, 1>(a, rows, resid, mod, s);
     else if (a.hidden <= 6144) q16_launch<3, 2>(a, rows, resid, mod, s);
     else q16_launch<4, 2>(a, rows, resid, mod, s);
+    return lr::launch_status("rms_adaln");
+  }
+  if (!quant && !resid && vec && !LR_K3R_OFF && a.hidden >= 2048 && a.hidden <= 8192 && a.hidden % 8 == 0) {
+    // K3 in the 8-column layout, one 128-thread CTA per row
+    const int c = (a.hidden + 2047) / 2048;
+    const unsigned grid = (unsigned)rows;
+#define LR_K3R(CC)                                                                                     \
+  if (mod) lr::rms_bf16_row_kernel<CC, true><<<grid, lr::kQ16Threads, 0, s>>>(a);                   \
+  else lr::rms_bf16_row_kernel<CC, false><<<grid, lr::kQ16Threads, 0, s>>>(a)
+    if (c <= 1) { LR_K3R(1); } else if (c == 2) { LR_K3R(2); } else if (c == 3) { LR_K3R(3); } else { LR_K3R(4); }
+#undef LR_K3R
     return lr::launch_status("rms_adaln");
   }
   const int C = pick_chunks(a.hidden);
