@@ -49,6 +49,10 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--tokens", type=int, default=12240,
                    help="block: token rows of the latent, sharded over the GPUs; flash: token rows per GPU")
+    p.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                   help="block workload at N > 1: 'peer' writes the FFN-down GEMM's output rows straight into every "
+                        "rank's gathered tensor over NVLink (the epilogue is the all-gather); 'nccl' runs "
+                        "all_gather_into_tensor after the block")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels", "kernel"],
@@ -136,7 +140,7 @@ def workload_config(args, world):
         "text_context": [W.TEXT_TOKENS, W.TEXT_DIM],
         "attention": "cores stubbed (self-attn returns V, cross-attn returns Q): out of scope",
         "parallelism": (f"{world} GPU(s): contiguous token-row shards, int8 weights replicated, "
-                        "one NCCL all_gather_into_tensor of the bf16 block output per step"
+                        "the bf16 block output all-gathered to every GPU each step"
                         if world > 1 else "1 GPU: all token rows, no collective"),
         "l2": "no flush: per-step working set (0.58 GB int8 weights + activations) >> 126 MB L2",
     }
@@ -345,15 +349,30 @@ def run_ours(args, rank, world, local):
     x_full, table, idx_full, ctx = block.make_inputs(total, seed=100, device=dev)  # same latent on every rank
     x = x_full[:, start_row:stop_row].contiguous()
     idx = idx_full[start_row:stop_row].contiguous()
-    gather = RowGather(total) if world > 1 else None
+    from lynnreal_omni_b200.parallel import PeerRows
+    peer = PeerRows(total, d, dev) if world > 1 and args.gather == "peer" else None
+    gather = RowGather(total) if world > 1 and peer is None else None
     out_buf = torch.empty(total, d, dtype=torch.bfloat16, device=dev) if gather else None
     torch.cuda.synchronize()
+    counter = [0]
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     def step(xin, ffn_ev=None, ag_ev=None, out=None):
+        if peer is not None:
+            # the FFN-down epilogue writes this rank's rows into every rank's
+            # buffer `slot`; the barrier after it makes all rows visible
+            slot = counter[0] & 1
+            counter[0] += 1
+            blk(xin, table, idx, ctx, ffn_events=ffn_ev, rows_to=peer.destinations(slot))
+            if ag_ev is not None:
+                ag_ev[0].record()
+            peer.barrier()
+            if ag_ev is not None:
+                ag_ev[1].record()
+            return peer.local[slot]
         h, _ = blk(xin, table, idx, ctx, ffn_events=ffn_ev)
         if gather is None:
             return h.view(m, d)
@@ -386,7 +405,7 @@ def run_ours(args, rank, world, local):
     clocks = sampler.stop() if sampler else None
     elapsed_ms = start.elapsed_time(end)
     ffn_ms = statistics.mean(a.elapsed_time(b) for a, b in ffn)
-    ag_ms = statistics.mean(a.elapsed_time(b) for a, b in ag) if gather else 0.0
+    ag_ms = statistics.mean(a.elapsed_time(b) for a, b in ag) if world > 1 else 0.0
     t = torch.tensor([elapsed_ms, ffn_ms, ag_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -395,7 +414,7 @@ def run_ours(args, rank, world, local):
 
     # the gathered rows equal the unsharded block (rows are independent)
     gathered_ok = None
-    if gather is not None:
+    if world > 1:
         ok = torch.tensor([1], device=dev)
         if rank == 0:
             ok[0] = int(torch.equal(out, blk(x_full, table, idx_full, ctx)[0].view(total, d)))
@@ -437,6 +456,8 @@ def run_ours(args, rank, world, local):
         out_h = [torch.empty(m, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
         def api(xd, cd):
+            if peer is not None:  # this rank's rows of the gathered output, copied out of the reused buffer
+                return step(xd)[start_row:stop_row].clone()
             h, _ = blk(xd, table, idx, cd)
             if gather is None:
                 return h.view(m, d)
@@ -453,7 +474,7 @@ def run_ours(args, rank, world, local):
         e2.record()
         torch.cuda.synchronize()
         barrier()
-        ok = torch.equal(out_h[(args.steps - 1) & 1], out[start_row:stop_row].cpu() if gather else out.cpu())
+        ok = torch.equal(out_h[(args.steps - 1) & 1], out[start_row:stop_row].cpu() if world > 1 else out.cpu())
         te = torch.tensor([s2.elapsed_time(e2)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
@@ -473,6 +494,11 @@ def run_ours(args, rank, world, local):
     ceiling = None
     if rank == 0:
         ceiling = int8_ceiling_cublaslt(m, W.HIDDEN, W.FFN, dev)
+    if peer is not None:
+        torch.cuda.synchronize()
+        barrier()
+        peer.close()
+        barrier()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -521,13 +547,19 @@ def run_ours(args, rank, world, local):
         "data": "synthetic (seeded; random-init int8 weights)",
         "config": workload_config(args, world),
         "block_tops": block_ops / (step_ms / 1e3) / 1e12,
-        "allgather": None if gather is None else {
+        "allgather": None if world == 1 else {
+            "mode": ("peer: the FFN-down GEMM epilogue stores its rows into every rank's gathered tensor over "
+                     "NVLink (lr_int8_gemm_rows_to), then one stream-ordered NCCL barrier"
+                     if peer is not None else "nccl: all_gather_into_tensor after the block"),
             "ms_per_step": ag_ms, "share_of_step": ag_ms / step_ms,
             "bytes_received_per_rank": (total - m) * d * 2,
-            "algbw_GBps": total * d * 2 / (ag_ms / 1e3) / 1e9,
-            "busbw_GBps": (world - 1) / world * total * d * 2 / (ag_ms / 1e3) / 1e9,
+            "algbw_GBps": total * d * 2 / (ag_ms / 1e3) / 1e9 if peer is None else None,
+            "busbw_GBps": (world - 1) / world * total * d * 2 / (ag_ms / 1e3) / 1e9 if peer is None else None,
             "gathered_matches_unsharded": gathered_ok,
-            "timing": "CUDA events around all_gather_into_tensor on the compute stream, mean over steps, max over ranks"},
+            "timing": ("CUDA events around the barrier after the fused GEMM (the transfer itself is inside the GEMM)"
+                       if peer is not None else
+                       "CUDA events around all_gather_into_tensor on the compute stream") +
+                      ", mean over steps, max over ranks"},
         "replica": replica,
         "roofline": roofline,
         "clocks": clocks,

@@ -271,6 +271,43 @@ int lr_int8_gemm_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_str
                     const int64_t* indices, int64_t sequence, int gate_slot, void* out,
                     int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* lr_int8_gemm whose output rows go to several places at once: the row m of
+ * the result is written to row row_offset + m of each of the
+ * `num_destinations` (1 to 8) bf16 matrices `destinations[d]` (leading
+ * dimension ld_destination), which may be other GPUs' memory mapped into this
+ * process (lr_ipc_import). No counterpart in the reference, which gathers
+ * sharded rows, if at all, with a separate collective: here the GEMM epilogue
+ * is the all-gather, its bulk tensor stores to every rank's copy of the
+ * gathered tensor overlapping the tensor-core work over NVLink. The kernel
+ * returns only once every store has landed; making the writes visible to the
+ * other GPUs' next kernels takes a cross-GPU barrier after it (an NCCL
+ * collective on the same stream), and no GPU may read or write the
+ * destination rows while the call runs. Needs the CTA-pair tensor-core path
+ * (K-major 16-byte aligned operands, M > 128), N a multiple of 32,
+ * ld_destination a multiple of 8 and 16-byte aligned destinations; otherwise
+ * LR_ERR_UNSUPPORTED. Epilogues and results as lr_int8_gemm (`out` is the
+ * destinations). */
+int lr_int8_gemm_rows_to(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                         int64_t b_stride_n, int64_t M, int64_t N, int64_t K, const float* row_scale,
+                         const float* col_scale, const void* bias, int epilogue, const void* resid,
+                         int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
+                         const int64_t* indices, int64_t sequence, int gate_slot,
+                         void* const* destinations, int num_destinations, int64_t ld_destination,
+                         int64_t row_offset, void* stream);
+
+/* CUDA IPC of device buffers between the processes of one node (one process
+ * per GPU), for lr_int8_gemm_rows_to's peer destinations. No counterpart in
+ * the reference (it has no multi-GPU code). lr_ipc_export writes the 64-byte
+ * handle of the cudaMalloc allocation holding `ptr` and ptr's offset in it;
+ * lr_ipc_import maps such a handle from another process on the current device
+ * and returns the pointer at `offset` (peer access enabled lazily);
+ * lr_ipc_release unmaps it. The exporting process must keep the buffer alive
+ * while others map it. */
+#define LR_IPC_HANDLE_BYTES 64
+int lr_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int lr_ipc_import(const void* handle, int64_t offset, void** ptr);
+int lr_ipc_release(void* ptr, int64_t offset);
+
 /* Size of the fixed split-K scratch array behind lr_int8_gemm_noalloc. */
 #define LR_NOALLOC_SCRATCH_BYTES (16ll << 20)
 

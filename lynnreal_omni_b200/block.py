@@ -94,7 +94,7 @@ class FlashBlockW8A8:
         return int8_matmul_gated_residual(q, layer.weight_int8, s, layer.weight_scale, layer.bias, residual,
                                           table, idx, slot, out=out)
 
-    def forward(self, x, table, indices, context, ffn_events=None, probe=None):
+    def forward(self, x, table, indices, context, ffn_events=None, probe=None, rows_to=None):
         """x bf16 [1, M, D] -> (x' bf16 [1, M, D], text K/V bf16 [T, 2D]).
 
         ``ffn_events`` (start, end) CUDA events, if given, bracket the FFN-up
@@ -104,6 +104,10 @@ class FlashBlockW8A8:
         and its gated residual), "cross" (after the cross-attention residual),
         "ffn_up" (the GELU-tanh output [M, FFN]). The residual stream is then
         updated in place, so a probe that keeps a tensor must copy it.
+        ``rows_to`` (pointers, ld, row_offset), if given, sends the block's
+        output rows from the FFN-down GEMM epilogue to those destinations
+        (``parallel.PeerRows``: every rank's gathered tensor) instead of the
+        residual stream; the first result is then None.
         """
         d = self.hidden
         note = probe or (lambda stage, t: None)
@@ -132,6 +136,10 @@ class FlashBlockW8A8:
             ffn_events[1].record()
         note("ffn_up", u)
         q, s = K.quantize_rows(u)
+        if rows_to is not None:
+            int8_matmul_gated_residual(q, self.down.weight_int8, s, self.down.weight_scale, self.down.bias, h,
+                                       table, indices, 5, rows_to=rows_to)
+            return None, kv
         self._gated(self.down, q, s, h, table, indices, 5, out=h)
         return h, kv
 

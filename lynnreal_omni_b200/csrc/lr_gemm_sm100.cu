@@ -36,6 +36,12 @@
 #ifndef LR_GEMM_STREAM_STORES  // 1: evict-first (st.global.cs) output stores
 #define LR_GEMM_STREAM_STORES 0
 #endif
+#ifndef LR_GEMM_TMA_OUT  // 1: the pair kernel stores bf16 outputs with bulk tensor stores
+#define LR_GEMM_TMA_OUT 1
+#endif
+#ifndef LR_GEMM_OUT_EVICT_FIRST  // L2 policy of those stores: 1 evict-first, 0 normal
+#define LR_GEMM_OUT_EVICT_FIRST 0
+#endif
 
 namespace lr {
 
@@ -359,10 +365,9 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
 // Epilogue of one W-column chunk of one row (W a multiple of 8), vectorised
 // (all W columns valid).
 template <int EPI, int W = 32>
-__device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[W],
-                                                int64_t row, int col0, float rs,
-                                                const bf16* gate_ptr, bool have_gate,
-                                                const uint4* resid_pre = nullptr) {
+__device__ __forceinline__ void chunk_values(const EpiArgs& ep, const uint32_t (&acc)[W], int64_t row,
+                                             int col0, float rs, const bf16* gate_ptr, bool have_gate,
+                                             const uint4* resid_pre, uint4 (&out)[W / 8]) {
   static_assert(W % 8 == 0, "chunk width");
   const float4* cs4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
   float d[W];
@@ -397,7 +402,6 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
       }
     }
   }
-  uint4* dst = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col0);
 #pragma unroll
   for (int q = 0; q < W / 8; ++q) {
     float o[8];
@@ -422,10 +426,24 @@ __device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_
                                 : make_uint4(gd, gd, gd, gd);
       y = badd8(x, bmul8(g, y));
     }
+    out[q] = y;
+  }
+}
+
+template <int EPI, int W = 32>
+__device__ __forceinline__ void store_chunk_vec(const EpiArgs& ep, const uint32_t (&acc)[W],
+                                                int64_t row, int col0, float rs,
+                                                const bf16* gate_ptr, bool have_gate,
+                                                const uint4* resid_pre = nullptr) {
+  uint4 y[W / 8];
+  chunk_values<EPI, W>(ep, acc, row, col0, rs, gate_ptr, have_gate, resid_pre, y);
+  uint4* dst = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col0);
+#pragma unroll
+  for (int q = 0; q < W / 8; ++q) {
     if (LR_GEMM_STREAM_STORES)
-      __stcs(dst + q, y);  // evict-first output stores
+      __stcs(dst + q, y[q]);  // evict-first output stores
     else
-      dst[q] = y;
+      dst[q] = y[q];
   }
 }
 
@@ -453,6 +471,107 @@ __device__ __forceinline__ void store_chunk_tail(const EpiArgs& ep, const uint32
                     : ((ep.table == nullptr) ? 1.0f : 0.0f);
     }
     reinterpret_cast<uint16_t*>(ep.out)[row * ep.ldo + col] = f2bf_bits(finish<EPI>(d, x, g));
+  }
+}
+
+// ------------------------------------------------- TMA-store epilogue
+// Output destinations of the bulk-tensor-store epilogue: bf16 matrices of M
+// rows x N columns (each map's base is already offset to the GEMM's first
+// row), box 32 columns x 32 rows, 64-byte swizzle. One destination is the
+// plain output; several are the same rows in every rank's copy of a gathered
+// tensor (peer memory mapped over NVLink), so the epilogue is also the
+// all-gather. Plain TMA stores, no multicast.
+constexpr int kMaxDst = 8;
+struct OutMaps {
+  CUtensorMap map[kMaxDst];
+  int count;
+};
+constexpr int kOutChunk = 32 * 32 * 2;               // one warp's 32 rows x 32 columns of bf16
+constexpr int kOutStage = NUM_EPI_WARPS * 2 * kOutChunk;  // double-buffered per epilogue warp
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most one committed group still reads shared memory
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// wait until every committed group has completed its writes
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Drain one accumulator as drain_accumulator does, but store each 32-column
+// chunk through shared memory with bulk tensor stores: the 32 lanes write
+// their rows into this warp's staging buffer (64-byte swizzle, so the 16-byte
+// writes are bank-conflict free), then lane 0 stores the 32 x 32 box to every
+// destination. Rows past M are clipped by the tensor maps. Requires N a
+// multiple of 32. `chunk` counts this warp's chunks (staging buffer parity).
+template <int EPI>
+__device__ __forceinline__ void drain_accumulator_tma(const EpiArgs& ep, const OutMaps& outs, int M, int N,
+                                                      uint32_t tbase, int64_t row0, int col_base, int lane,
+                                                      uint32_t release_bar, uint8_t* staging, uint32_t& chunk,
+                                                      uint64_t policy) {
+  const int64_t row = row0 + lane;
+  const bool row_ok = row < M;
+  float rs = 0.0f;
+  const bf16* gptr = nullptr;
+  bool have_gate = false;
+  if (row_ok) {
+    rs = ep.row_scale[row];
+    if (EPI == kGated && ep.table != nullptr) {
+      bool bad;
+      const bf16* g = gate_row(ep, row, bad);
+      if (bad) atomicOr(&g_gemm_status, (unsigned)kDevErrTableIndex);
+      if (g != nullptr) {
+        gptr = g + (int64_t)ep.gate_slot * N;
+        have_gate = true;
+      }
+    }
+  }
+  uint4 xr[4] = {}, xn[4] = {};
+  auto load_resid = [&](int c, uint4 (&dst)[4]) {
+    if (row_ok) {
+      const uint4* src = reinterpret_cast<const uint4*>(ep.resid + row * ep.ldr + col_base + c * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = src[q];
+    }
+  };
+  if (EPI == kGated) load_resid(0, xr);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    if (EPI == kGated && c + 1 < BN / 32) load_resid(c + 1, xn);
+    uint32_t r[32];
+    tmem_ld32(tbase + (uint32_t)(c * 32), r);
+    if (c == BN / 32 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(release_bar, 0u);
+    }
+    const int col0 = col_base + c * 32;
+    if (col0 >= N) continue;
+    uint4 y[4];
+    chunk_values<EPI>(ep, r, row, col0, rs, gptr, have_gate, EPI == kGated ? xr : nullptr, y);
+    uint8_t* buf = staging + (chunk & 1u) * kOutChunk;
+    if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = y[q];
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t src = smem_u32(buf);
+      for (int d = 0; d < outs.count; ++d) tma_store_2d(&outs.map[d], src, col0, (int)row0, policy);
+      bulk_commit();
+    }
+    ++chunk;
+    if (EPI == kGated) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xr[q] = xn[q];
+    }
   }
 }
 
@@ -710,12 +829,15 @@ constexpr int STAGES2 = LR_GEMM_STAGES2;
 constexpr int A2_STAGE = 128 * BK;
 constexpr int B2_STAGE = 128 * BK;
 constexpr size_t SMEM2_BYTES = 1024 + (size_t)STAGES2 * (A2_STAGE + B2_STAGE) + BAR_BYTES;
+// with the bulk-tensor-store epilogue: the staging buffers start 1 KB past the
+// barriers (1024-aligned, as the 64-byte swizzle pattern needs 512)
+constexpr size_t SMEM2_OUT_BYTES = 1024 + (size_t)STAGES2 * (A2_STAGE + B2_STAGE) + 1024 + kOutStage;
 
-template <int EPI>
+template <int EPI, bool TMA_OUT = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b, int M, int N, int K, int group_m,
-                    int splits, const EpiArgs ep) {
+                    int splits, const EpiArgs ep, const __grid_constant__ OutMaps outs) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -729,6 +851,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain = bars + 2 * STAGES2 + 2 * NUM_ACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  // TMA_OUT: per-epilogue-warp double-buffered output staging, 1024-aligned
+  uint8_t* out_stage = reinterpret_cast<uint8_t*>(bars) + 1024;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -864,6 +988,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // -------------------------------------------- epilogue warps (both CTAs)
     const int quad = warp & 3;
+    uint8_t* staging = out_stage + (warp - 2) * 2 * kOutChunk;
+    uint32_t chunk = 0;
+    const uint64_t out_policy = LR_GEMM_OUT_EVICT_FIRST ? l2_policy_evict_first() : l2_policy_evict_normal();
     int local = 0;
     for (int w = cluster_id; w < work; w += clusters, ++local) {
       const int t = w / splits;
@@ -877,10 +1004,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int mb, nb;
       tile_coords(t, num_m, num_n, group_m, mb, nb);
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      EpiArgs epw = ep;
-      if (EPI == kS32Part) epw.acc_out = ep.acc_out + (int64_t)(w - t * splits) * M * N;
-      drain_accumulator<EPI>(epw, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32 + lane,
-                             nb * BN, lane, smem_u32(&tempty[acc]), 0, true);
+      if constexpr (TMA_OUT) {
+        drain_accumulator_tma<EPI>(ep, outs, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32, nb * BN, lane,
+                                   smem_u32(&tempty[acc]), staging, chunk, out_policy);
+      } else {
+        EpiArgs epw = ep;
+        if (EPI == kS32Part) epw.acc_out = ep.acc_out + (int64_t)(w - t * splits) * M * N;
+        drain_accumulator<EPI>(epw, M, N, tbase, (int64_t)mb * 256 + rank * 128 + quad * 32 + lane,
+                               nb * BN, lane, smem_u32(&tempty[acc]), 0, true);
+      }
+    }
+    if (TMA_OUT && lane == 0) {
+      // every bulk store of this warp has written its destinations (local or
+      // peer memory) before the kernel can complete
+      bulk_wait_all();
+      __threadfence_system();
     }
   }
 
@@ -1032,6 +1170,31 @@ int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
   return LR_OK;
 }
 
+// bf16 destination map of the bulk-store epilogue: M rows x N columns from
+// `base`, rows `ld` elements apart, box 32 columns x 32 rows, 64-byte swizzle.
+int make_out_map(CUtensorMap* map, const void* base, int64_t M, int64_t N, int64_t ld) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(LR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LR_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return LR_OK;
+}
+
+// Where the bulk-store epilogue writes: `count` bf16 matrices (leading
+// dimension `ld`), the GEMM's row m landing on row row_offset + m of each.
+struct Destinations {
+  void* const* ptrs;
+  int count;
+  int64_t ld;
+  int64_t row_offset;
+};
+
 // M-blocks per raster group: as many as keep the group's A panel (rows x K
 // bytes) within a quarter-to-half of the 126 MB L2, so the weights stream
 // from HBM about once per group.
@@ -1077,24 +1240,53 @@ int launch_tc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M,
   return launch_status("int8 gemm (tcgen05)");
 }
 
-// CTA-pair tensor-core kernel: 256x256 tiles over clusters of two CTAs.
+// CTA-pair tensor-core kernel: 256x256 tiles over clusters of two CTAs. With
+// `dst` (or, for the bf16 epilogues, whenever N is a multiple of 32 and the
+// output allows 16-byte rows) the epilogue stores through shared memory with
+// bulk tensor stores; `dst` may name several destinations (see Destinations).
 template <int EPI>
 int launch_tc2(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N, int K,
-               const EpiArgs& ep, cudaStream_t stream) {
+               const EpiArgs& ep, cudaStream_t stream, const Destinations* dst = nullptr) {
   CUtensorMap ma, mb;
   int st = make_map(&ma, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 128);
   if (st) return st;
   st = make_map(&mb, b, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 128);
   if (st) return st;
-  static bool done[64] = {};
-  st = configure_smem(gemm_tc2_kernel<EPI>, SMEM2_BYTES, done);
-  if (st) return st;
   const int num_m = (M + 255) / 256;
   const int tiles = num_m * ((N + BN - 1) / BN);
   const int pairs = sm_count() / 2;
   const int clusters = tiles < pairs ? tiles : pairs;
-  gemm_tc2_kernel<EPI><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(
-      ma, mb, M, N, K, raster_group(256, num_m, K), 1, ep);
+  const int group = raster_group(256, num_m, K);
+  if constexpr (EPI == kNone || EPI == kGelu || EPI == kGated) {
+    const bool tma = dst != nullptr || (LR_GEMM_TMA_OUT && N % 32 == 0 && ep.ldo % 8 == 0 && aligned(ep.out, 16));
+    if (tma) {
+      OutMaps outs{};
+      if (dst != nullptr) {
+        for (int d = 0; d < dst->count; ++d) {
+          const bf16* base = static_cast<const bf16*>(dst->ptrs[d]) + dst->row_offset * dst->ld;
+          st = make_out_map(&outs.map[d], base, M, N, dst->ld);
+          if (st) return st;
+        }
+        outs.count = dst->count;
+      } else {
+        st = make_out_map(&outs.map[0], ep.out, M, N, ep.ldo);
+        if (st) return st;
+        outs.count = 1;
+      }
+      static bool done_tma[64] = {};
+      st = configure_smem(gemm_tc2_kernel<EPI, true>, SMEM2_OUT_BYTES, done_tma);
+      if (st) return st;
+      gemm_tc2_kernel<EPI, true><<<2 * clusters, NUM_THREADS, SMEM2_OUT_BYTES, stream>>>(ma, mb, M, N, K, group, 1,
+                                                                                        ep, outs);
+      return launch_status("int8 gemm (tcgen05, CTA pair, bulk-store epilogue)");
+    }
+  }
+  if (dst != nullptr) return set_error(LR_ERR_UNSUPPORTED, "int8 gemm: this epilogue has no multi-destination form");
+  static bool done[64] = {};
+  st = configure_smem(gemm_tc2_kernel<EPI>, SMEM2_BYTES, done);
+  if (st) return st;
+  const OutMaps none{};
+  gemm_tc2_kernel<EPI><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(ma, mb, M, N, K, group, 1, ep, none);
   return launch_status("int8 gemm (tcgen05, CTA pair)");
 }
 
@@ -1120,6 +1312,9 @@ template <int EPI>
 int launch_tc2_splitk(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int M, int N,
                       int K, int splits, int32_t* ws, const EpiArgs& ep, bool vec,
                       cudaStream_t stream) {
+  // the finishing kernel's 16-byte accesses: checked before anything launches
+  if (!vec || N % 8 != 0 || !aligned(ws, 16))
+    return set_error(LR_ERR_UNSUPPORTED, "int8 gemm split-K: output not vectorisable");
   CUtensorMap ma, mb;
   int st = make_map(&ma, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 128);
   if (st) return st;
@@ -1134,12 +1329,11 @@ int launch_tc2_splitk(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb
   const int work = num_m * ((N + BN - 1) / BN) * splits;
   const int pairs = sm_count() / 2;
   const int clusters = work < pairs ? work : pairs;
+  const OutMaps none{};
   gemm_tc2_kernel<kS32Part><<<2 * clusters, NUM_THREADS, SMEM2_BYTES, stream>>>(
-      ma, mb, M, N, K, raster_group(256, num_m, K), splits, acc);
+      ma, mb, M, N, K, raster_group(256, num_m, K), splits, acc, none);
   st = launch_status("int8 gemm (tcgen05, CTA pair, split-K)");
   if (st) return st;
-  if (!vec || N % 8 != 0 || !aligned(ws, 16))
-    return set_error(LR_ERR_UNSUPPORTED, "int8 gemm split-K: output not vectorisable");
   const dim3 grid((unsigned)M, (unsigned)((N / 8 + 255) / 256));
   splitk_epilogue_kernel<EPI><<<grid, 256, 0, stream>>>(ws, M, N, splits, ep);
   return launch_status("int8 gemm split-K epilogue");
@@ -1157,9 +1351,16 @@ int launch_simt(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int6
 template <int EPI>
 int run(const int8_t* a, int64_t lda, const int8_t* b, int64_t bsk, int64_t bsn, int64_t M,
         int64_t N, int64_t K, const EpiArgs& ep, bool out_vec_ok, cudaStream_t stream,
-        int32_t* ws = nullptr, int64_t ws_bytes = 0) {
+        int32_t* ws = nullptr, int64_t ws_bytes = 0, const Destinations* dst = nullptr) {
   const bool tc = bsk == 1 && K > 0 && lda % 16 == 0 && bsn % 16 == 0 && aligned(a, 16) &&
                   aligned(b, 16) && out_vec_ok;
+  if (dst != nullptr) {
+    if (!tc || M <= BM || N % 32 != 0)
+      return set_error(LR_ERR_UNSUPPORTED,
+                       "int8 gemm to several destinations needs the CTA-pair tensor-core path "
+                       "(K-major 16-byte operands, M > %d, N a multiple of 32)", BM);
+    return launch_tc2<EPI>(a, lda, b, bsn, (int)M, (int)N, (int)K, ep, stream, dst);
+  }
   if constexpr (EPI != kS32) {
     if (tc && ws != nullptr) {
       const int splits = splitk_slices(M, N, K);
@@ -1210,7 +1411,8 @@ static int gemm_entry(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_s
                       const float* col_scale, const void* bias, int epilogue, const void* resid,
                       int64_t ldr, const void* table, int64_t table_rows, int64_t table_width,
                       const int64_t* indices, int64_t sequence, int gate_slot, void* out,
-                      int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream) {
+                      int64_t ldo, void* workspace, int64_t workspace_bytes, void* stream,
+                      const lr::gemm::Destinations* dst = nullptr) {
   using namespace lr::gemm;
   int st = check_gemm_shape("int8_gemm", a, lda, b, b_stride_k, b_stride_n, M, N, K);
   if (st) return st;
@@ -1253,12 +1455,37 @@ static int gemm_entry(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_s
   int32_t* ws = static_cast<int32_t*>(workspace);
   switch (epilogue) {
     case LR_EPI_GELU_TANH:
-      return run<kGelu>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
+      return run<kGelu>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes, dst);
     case LR_EPI_GATED_RESIDUAL:
-      return run<kGated>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
+      return run<kGated>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes, dst);
     default:
-      return run<kNone>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes);
+      return run<kNone>(a, lda, b, b_stride_k, b_stride_n, M, N, K, ep, vec, s, ws, workspace_bytes, dst);
   }
+}
+
+extern "C" int lr_int8_gemm_rows_to(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,
+                                    int64_t b_stride_n, int64_t M, int64_t N, int64_t K,
+                                    const float* row_scale, const float* col_scale, const void* bias,
+                                    int epilogue, const void* resid, int64_t ldr, const void* table,
+                                    int64_t table_rows, int64_t table_width, const int64_t* indices,
+                                    int64_t sequence, int gate_slot, void* const* destinations,
+                                    int num_destinations, int64_t ld_destination, int64_t row_offset,
+                                    void* stream) {
+  LR_REQUIRE(num_destinations >= 1 && num_destinations <= lr::gemm::kMaxDst,
+             "int8_gemm_rows_to: %d destinations (1 to %d)", num_destinations, lr::gemm::kMaxDst);
+  LR_REQUIRE(destinations != nullptr, "int8_gemm_rows_to: null destination list");
+  LR_REQUIRE(ld_destination >= N && ld_destination % 8 == 0 && row_offset >= 0,
+             "int8_gemm_rows_to: ld_destination %lld (>= N, a multiple of 8) / row_offset %lld",
+             (long long)ld_destination, (long long)row_offset);
+  for (int d = 0; d < num_destinations; ++d)
+    LR_REQUIRE(destinations[d] != nullptr && lr::aligned(destinations[d], 16),
+               "int8_gemm_rows_to: destination %d is null or not 16-byte aligned", d);
+  if (M == 0) return LR_OK;
+  const lr::gemm::Destinations dst{destinations, num_destinations, ld_destination, row_offset};
+  void* first = static_cast<__nv_bfloat16*>(destinations[0]) + row_offset * ld_destination;
+  return gemm_entry(a, lda, b, b_stride_k, b_stride_n, M, N, K, row_scale, col_scale, bias, epilogue, resid,
+                    ldr, table, table_rows, table_width, indices, sequence, gate_slot, first, ld_destination,
+                    nullptr, 0, stream, &dst);
 }
 
 extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t b_stride_k,

@@ -1,5 +1,6 @@
 // Host-side plumbing of the C ABI: error messages, launch status, SM count and
 // the device status word.
+#include <cuda.h>
 #include <string.h>
 
 #include "lr_host.h"
@@ -60,4 +61,62 @@ extern "C" int lr_device_status(unsigned int* bits, int clear) {
   st = lr::read_status_flash(bits, clear);
   if (st) return st;
   return lr::read_status_attention(bits, clear);
+}
+
+// ------------------------------------------------------------- CUDA IPC
+// Peer mapping of device buffers between the processes of one node (one
+// process per GPU): a buffer is exported as the IPC handle of the allocation
+// that holds it plus its offset in that allocation, and imported by mapping
+// the allocation (peer access over NVLink enabled lazily).
+namespace {
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+static_assert(sizeof(cudaIpcMemHandle_t) == LR_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int lr_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  LR_REQUIRE(ptr != nullptr && handle != nullptr && offset != nullptr, "ipc_export: null argument");
+  auto range = address_range_fn();
+  if (range == nullptr) return lr::set_error(LR_ERR_CUDA, "ipc_export: cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return lr::set_error(LR_ERR_INVALID_ARGUMENT, "ipc_export: %p is not device memory of this context", ptr);
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess)
+    return lr::launch_status("ipc_export: cudaIpcGetMemHandle (the allocation must come from cudaMalloc)");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return LR_OK;
+}
+
+extern "C" int lr_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  LR_REQUIRE(handle != nullptr && ptr != nullptr && offset >= 0, "ipc_import: invalid argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return lr::launch_status("ipc_import: cudaIpcOpenMemHandle");
+  *ptr = static_cast<char*>(base) + offset;
+  return LR_OK;
+}
+
+extern "C" int lr_ipc_release(void* ptr, int64_t offset) {
+  LR_REQUIRE(ptr != nullptr && offset >= 0, "ipc_release: invalid argument");
+  if (cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset) != cudaSuccess)
+    return lr::launch_status("ipc_release: cudaIpcCloseMemHandle");
+  return LR_OK;
 }

@@ -15,6 +15,8 @@ fused into the epilogue).
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -47,7 +49,7 @@ def _scales(row_scale, column_scale, m: int, n: int):
 
 
 def _launch(a, b, row_scale, column_scale, bias, epilogue, residual=None, table=None, indices=None,
-            gate_slot=0, out=None):
+            gate_slot=0, out=None, rows_to=None):
     _contract(a, b)
     m, k = a.shape
     n = b.shape[1]
@@ -55,7 +57,8 @@ def _launch(a, b, row_scale, column_scale, bias, epilogue, residual=None, table=
     bb = None if bias is None else bias.to(torch.bfloat16).contiguous()
     if bb is not None and bb.numel() != n:
         raise ValueError("INT8 GEMM bias must have N elements")
-    output = torch.empty((m, n), device=a.device, dtype=torch.bfloat16) if out is None else out
+    output = None if rows_to is not None else (
+        torch.empty((m, n), device=a.device, dtype=torch.bfloat16) if out is None else out)
     resid_ptr, ldr, tbl, trows, twidth, idx, seq = None, 0, None, 0, 0, None, 1
     if epilogue == _lib.LR_EPI_GATED_RESIDUAL:
         res = residual.reshape(-1, residual.shape[-1])
@@ -73,6 +76,14 @@ def _launch(a, b, row_scale, column_scale, bias, epilogue, residual=None, table=
             if idx.numel() < seq:
                 raise ValueError(f"expected at least {seq} adaLN indices, got {idx.numel()}")
     lib = _lib.load()
+    if rows_to is not None:
+        ptrs, ld, row_offset = rows_to
+        arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+        check(lib.lr_int8_gemm_rows_to(
+            ptr(a), a.stride(0), ptr(b), b.stride(0), b.stride(1), m, n, k, ptr(rs), ptr(cs), ptr(bb), epilogue,
+            resid_ptr, ldr, ptr(tbl), trows, twidth, ptr(idx), seq, gate_slot, arr, len(ptrs), ld, row_offset,
+            stream_of(a)), "int8_matmul (rows to destinations)")
+        return None
     ws_bytes = lib.lr_int8_gemm_workspace_bytes(m, n, k)
     # small-M shapes split K across the GPU: the int32 partial-sum workspace
     # comes from torch's caching allocator (the library allocates nothing)
@@ -104,18 +115,22 @@ def int8_matmul_gelu(a, b, row_scale, column_scale, bias=None):
 
 
 def int8_matmul_gated_residual(a, b, row_scale, column_scale, bias, residual, table, indices,
-                               gate_slot, out=None):
+                               gate_slot, out=None, rows_to=None):
     """``_gated_residual(residual, int8_matmul(...), table, indices, gate_slot)`` in one kernel.
 
     Row r of the output uses table row ``indices[r % S]`` with S = residual.shape[-2];
     ``table=None`` means gate 1 (a plain bf16 residual add). ``out`` may be
     ``residual`` itself (in-place update of the residual stream).
+    ``rows_to=(pointers, ld, row_offset)`` sends the output rows instead to row
+    ``row_offset + r`` of each bf16 matrix at ``pointers`` (device addresses,
+    possibly other GPUs' memory mapped by ``parallel.PeerRows``; leading
+    dimension ``ld``) and returns None: the GEMM epilogue is the all-gather.
     """
     res_shape = residual.shape
     out2 = None if out is None else out.view(-1, out.shape[-1])
     y = _launch(a, b, row_scale, column_scale, bias, _lib.LR_EPI_GATED_RESIDUAL, residual, table,
-                indices, gate_slot, out2)
-    return y.view(res_shape)
+                indices, gate_slot, out2, rows_to)
+    return None if y is None else y.view(res_shape)
 
 
 def int8_matmul_s32(a, b):

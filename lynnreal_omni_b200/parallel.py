@@ -6,8 +6,17 @@ block with the int8 weights replicated, and the only collective is one
 all-gather of the bf16 output rows at the end (NCCL over NVLink/NVSwitch on a
 B200 node). Shards differ by at most one row; the gather pads every shard to
 the largest one and strips the padding afterwards.
+
+``PeerRows`` replaces that collective where the last projection of the path
+can write its rows itself: every rank's copy of the gathered tensor is mapped
+into every other rank (CUDA IPC, peer access over NVLink), and the projection's
+GEMM epilogue stores each output tile into all of them
+(``int8_matmul_gated_residual(..., rows_to=...)``), so the transfer overlaps
+the tensor-core work instead of following it.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -89,3 +98,68 @@ def gather_rows(local: torch.Tensor, total: int, group=None, bounds=None) -> tor
     rank (see ``RowGather``).
     """
     return RowGather(total, group, bounds)(local)
+
+
+class PeerRows:
+    """Gathered ``[total, width]`` bf16 tensors that a GEMM epilogue fills on
+    every rank at once.
+
+    Each rank allocates ``buffers`` such tensors, exports their CUDA IPC
+    handles and maps every other rank's, so ``destinations(i)`` lists the
+    device addresses of buffer ``i`` on all ranks (rank order), usable as the
+    ``rows_to`` pointers of ``int8_gemm`` calls; this rank's rows start at
+    ``row_offset``. Buffers alternate between steps so that one step's rows
+    can be read while the next is written. ``barrier()`` is a stream-ordered
+    cross-GPU barrier (an NCCL all-reduce of one element on the current
+    stream): once it has run on every rank after the writing kernels, all
+    ranks' rows are visible; before the next write into a buffer it also
+    tells every writer that its readers are done with it.
+    """
+
+    def __init__(self, total: int, width: int, device, group=None, buffers: int = 2):
+        from . import _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.total, self.width = total, width
+        start, stop = shard_bounds(total, self.world, self.rank)
+        self.row_offset, self.rows = start, stop - start
+        self.lib = _lib.load()
+        self.local = [torch.empty(total, width, dtype=torch.bfloat16, device=device) for _ in range(buffers)]
+        exported = []
+        for t in self.local:
+            handle = ctypes.create_string_buffer(64)
+            offset = ctypes.c_int64(0)
+            _lib.check(self.lib.lr_ipc_export(t.data_ptr(), handle, ctypes.byref(offset)), "PeerRows: export")
+            exported.append((handle.raw, offset.value))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, exported, group=group)
+        self.mapped = []  # (pointer, offset) of every imported peer buffer, for release
+        self.pointers = []
+        for i in range(buffers):
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self.local[i].data_ptr())
+                    continue
+                raw, offset = everyone[r][i]
+                out = ctypes.c_void_p(0)
+                _lib.check(self.lib.lr_ipc_import(raw, offset, ctypes.byref(out)), "PeerRows: import")
+                self.mapped.append((out.value, offset))
+                ptrs.append(out.value)
+            self.pointers.append(ptrs)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def destinations(self, slot: int):
+        """``rows_to`` argument for buffer ``slot``: (pointers, ld, row_offset)."""
+        return self.pointers[slot], self.width, self.row_offset
+
+    def barrier(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        from . import _lib
+        for p, offset in self.mapped:
+            _lib.check(self.lib.lr_ipc_release(p, offset), "PeerRows: release")
+        self.mapped.clear()
+        self.pointers.clear()

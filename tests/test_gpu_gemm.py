@@ -280,3 +280,40 @@ def test_split_k_gelu_matches_unsplit_bits():
                                 None, 0, 0, None, 1, 0, out.data_ptr(), n,
                                 torch.cuda.current_stream().cuda_stream), "gemm")
     assert torch.equal(out, split)
+
+
+@pytest.mark.parametrize("m,k,n,epi", [(300, 512, 1024, "none"), (1530, 6144, 6144, "gated"), (129, 256, 512, "gelu")])
+def test_rows_to_several_destinations(m, k, n, epi):
+    """lr_int8_gemm_rows_to writes the GEMM's row r to row row_offset + r of
+    every destination (here two buffers of this GPU) and nothing else; the
+    rows equal lr_int8_gemm's output bit for bit."""
+    from lynnreal_omni_b200.int8_gemm import _launch
+    a, b, rs, cs, bias = workloads.gemm_operands(m, k, n, seed=m + n, bias=True, device=DEV)
+    gen = torch.Generator(device=DEV).manual_seed(m)
+    total, offset = m + 77, 41
+    resid = torch.randn(m, n, generator=gen, device=DEV).to(torch.bfloat16)
+    table = (0.3 * torch.randn(2, 6 * n, generator=gen, device=DEV)).to(torch.bfloat16)
+    idx = torch.randint(0, 2, (m,), generator=gen, device=DEV)
+    code = {"none": _lib.LR_EPI_NONE, "gelu": _lib.LR_EPI_GELU_TANH, "gated": _lib.LR_EPI_GATED_RESIDUAL}[epi]
+    extra = (resid, table, idx, 5) if epi == "gated" else ()
+    expect = _launch(a, b, rs, cs, bias, code, *extra)
+    dst = [torch.full((total, n + 8), -7.0, dtype=torch.bfloat16, device=DEV) for _ in range(2)]
+    ret = _launch(a, b, rs, cs, bias, code, *extra, rows_to=([t.data_ptr() for t in dst], n + 8, offset))
+    assert ret is None
+    for t in dst:
+        assert torch.equal(t[offset:offset + m, :n], expect)
+        untouched = torch.ones(total, n + 8, dtype=torch.bool, device=DEV)
+        untouched[offset:offset + m, :n] = False
+        assert bool((t[untouched] == -7.0).all())
+
+
+def test_rows_to_refuses_shapes_off_the_pair_path():
+    from lynnreal_omni_b200.int8_gemm import _launch
+    a, b, rs, cs, _ = workloads.gemm_operands(64, 256, 512, seed=3, device=DEV)
+    dst = torch.zeros(64, 512, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):  # M <= 128 runs the single-CTA kernel
+        _launch(a, b, rs, cs, None, _lib.LR_EPI_NONE, rows_to=([dst.data_ptr()], 512, 0))
+    a, b, rs, cs, _ = workloads.gemm_operands(300, 256, 520, seed=3, device=DEV)
+    dst = torch.zeros(300, 520, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):  # N not a multiple of 32
+        _launch(a, b, rs, cs, None, _lib.LR_EPI_NONE, rows_to=([dst.data_ptr()], 520, 0))
