@@ -308,6 +308,17 @@ int lr_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int lr_ipc_import(const void* handle, int64_t offset, void** ptr);
 int lr_ipc_release(void* ptr, int64_t offset);
 
+/* Test hook of the GEMM's bounded waits (no counterpart in the reference):
+ * sets, on the current device, the limit of every mbarrier wait of the
+ * tensor-core GEMM kernels (limit_ns; 0 restores the default of 2 s) and,
+ * with drop_first_load != 0, makes the next launch of the CTA-pair kernel
+ * skip one TMA load of its first stage, so that stage's barrier never
+ * completes. That launch's waits then run out: the kernel raises device status
+ * bit 1, drains its own copies and tensor-core work, frees its tensor memory
+ * and returns after a few limits; its output is unspecified. Later launches
+ * are unaffected. Not for production use. */
+int lr_gemm_test_wait(int64_t limit_ns, int drop_first_load);
+
 /* Size of the fixed split-K scratch array behind lr_int8_gemm_noalloc. */
 #define LR_NOALLOC_SCRATCH_BYTES (16ll << 20)
 
@@ -323,7 +334,11 @@ int lr_ipc_release(void* ptr, int64_t offset);
  *     rejected with LR_ERR_UNSUPPORTED (use lr_int8_gemm_ws with a workspace).
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *     before any stream capture. Under CUDA's lazy module loading (the
+ *     default) that first call, or the library's first kernel launch on the
+ *     device, is also when the GPU code is loaded and the 16 MiB array
+ *     allocated: make it at set-up time, not inside a step whose memory must
+ *     not grow. Later calls allocate nothing.
  *   - All calls share the one array and it keeps the last call's contents;
  *     nothing in it needs to start at zero (each call writes every element it
  *     later reads). Calls that overlap on the GPU (concurrent streams, or

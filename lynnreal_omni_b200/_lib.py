@@ -61,6 +61,7 @@ SIGNATURES = {
     "lr_int8_gemm_s32": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p], _i32),
     "lr_int8_gemm_rows_to": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p,
                               _i64, _i64, _p, _i64, _i32, _p, _i32, _i64, _i64, _p], _i32),
+    "lr_gemm_test_wait": ([_i64, _i32], _i32),
     "lr_ipc_export": ([_p, _p, ctypes.POINTER(ctypes.c_int64)], _i32),
     "lr_ipc_import": ([_p, _i64, ctypes.POINTER(ctypes.c_void_p)], _i32),
     "lr_ipc_release": ([_p, _i64], _i32),

@@ -46,6 +46,11 @@
 namespace lr {
 
 static __device__ unsigned int g_gemm_status = 0;
+// Limit of every mbarrier wait of the tensor-core kernels (lr_gemm_test_wait
+// shortens it) and a one-shot request to drop one TMA load (tests of the
+// bounded waits; see lr_gemm_test_wait).
+static __device__ unsigned long long g_gemm_wait_limit_ns = 2000000000ull;
+static __device__ unsigned int g_gemm_drop_load = 0;
 
 namespace gemm {
 
@@ -64,7 +69,7 @@ constexpr int NUM_EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * (A_STAGE + B_STAGE) + BAR_BYTES;
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s, the default wait limit
 
 // kS32: store raw int32 accumulators ([M, N], row stride N); kS32Part: store a
 // K slice's partial accumulators into its own [M, N] plane of the split-K
@@ -179,10 +184,11 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
                                              volatile uint32_t* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
+  const unsigned long long limit = g_gemm_wait_limit_ns;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       *abort_flag = 1u;
       atomicOr(&g_gemm_status, (unsigned)kDevErrWaitTimeout);
       return false;
@@ -288,10 +294,11 @@ __device__ __forceinline__ bool wait_bounded_cluster(uint32_t bar, uint32_t pari
                                                      volatile uint32_t* abort_flag) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
+  const unsigned long long limit = g_gemm_wait_limit_ns;
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       *abort_flag = 1u;
       atomicOr(&g_gemm_status, (unsigned)kDevErrWaitTimeout);
       return false;
@@ -739,7 +746,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (issued[s]) {
             const unsigned long long t0 = globaltimer();
             while (!mbar_try_wait(smem_u32(&full[s]), issued_phase[s]) &&
-                   globaltimer() - t0 < kWaitLimitNs / 4) {
+                   globaltimer() - t0 < g_gemm_wait_limit_ns / 4) {
             }
           }
       }
@@ -784,7 +791,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Abort: wait for the MMAs already issued before TMEM is released.
         mma_commit(smem_u32(drain));
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
+        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < g_gemm_wait_limit_ns / 4) {
         }
       }
     }
@@ -906,6 +913,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
+      // test of the bounded waits: the leader of cluster 0 skips one A load,
+      // so that stage's barrier never completes (one launch only)
+      bool drop = leader && cluster_id == 0 && atomicExch(&g_gemm_drop_load, 0u) != 0u;
       for (int w = cluster_id; w < work && ok; w += clusters) {
         const int t = w / splits;
         const int kb0 = (w - t * splits) * kper;
@@ -920,8 +930,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = smem_u32(&full[stage]);
           if (leader) mbar_expect_tx(fb, 2 * (A2_STAGE + B2_STAGE));
           const uint32_t fb_leader = map_to_rank(fb, 0);
-          tma_load_2d_pair(smem_u32(sa + stage * A2_STAGE), &map_a, fb_leader, kb * BK,
-                           mb * 256 + (int)rank * 128, pol_a);
+          if (drop)
+            drop = false;
+          else
+            tma_load_2d_pair(smem_u32(sa + stage * A2_STAGE), &map_a, fb_leader, kb * BK,
+                             mb * 256 + (int)rank * 128, pol_a);
           tma_load_2d_pair(smem_u32(sb + stage * B2_STAGE), &map_b, fb_leader, kb * BK,
                            nb * BN + (int)rank * 128, pol_b);
           issued_any = true;
@@ -981,7 +994,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!ok) {
         mma_commit_pair(smem_u32(drain), (uint16_t)0x1);
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < kWaitLimitNs / 4) {
+        while (!mbar_try_wait(smem_u32(drain), 0u) && globaltimer() - t0 < g_gemm_wait_limit_ns / 4) {
         }
       }
     }
@@ -1497,6 +1510,16 @@ extern "C" int lr_int8_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64
   return gemm_entry(a, lda, b, b_stride_k, b_stride_n, M, N, K, row_scale, col_scale, bias,
                     epilogue, resid, ldr, table, table_rows, table_width, indices, sequence,
                     gate_slot, out, ldo, nullptr, 0, stream);
+}
+
+extern "C" int lr_gemm_test_wait(int64_t limit_ns, int drop_first_load) {
+  LR_REQUIRE(limit_ns >= 0 && limit_ns <= 60ll * 1000000000ll, "gemm_test_wait: limit %lld ns", (long long)limit_ns);
+  const unsigned long long limit = limit_ns > 0 ? (unsigned long long)limit_ns : lr::gemm::kWaitLimitNs;
+  const unsigned int drop = drop_first_load ? 1u : 0u;
+  if (cudaMemcpyToSymbol(lr::g_gemm_wait_limit_ns, &limit, sizeof(limit)) != cudaSuccess ||
+      cudaMemcpyToSymbol(lr::g_gemm_drop_load, &drop, sizeof(drop)) != cudaSuccess)
+    return lr::launch_status("gemm_test_wait");
+  return LR_OK;
 }
 
 extern "C" int64_t lr_int8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {

@@ -89,3 +89,22 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     st = _gemm("lr_int8_gemm_noalloc", a, b, rs, cs, bias, out)
     assert st == _lib.LR_ERR_UNSUPPORTED
     assert b"static maximum" in lib.lr_last_error()
+
+
+def test_noalloc_calls_leave_free_device_memory_unchanged():
+    """After a first call (which may load the library's GPU code, and with it
+    the scratch array, under CUDA's lazy module loading), further calls change
+    the device's free memory by nothing: they allocate nothing."""
+    lib = _lib.load()
+    m, k, n = 128, 6144, 6144
+    assert lib.lr_int8_gemm_workspace_bytes(m, n, k) > 0  # takes the split-K scratch
+    a, b, rs, cs, bias = _operands(m, k, n, seed=34)
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    _lib.check(_gemm("lr_int8_gemm_noalloc", a, b, rs, cs, bias, out), "lr_int8_gemm_noalloc")
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(2):
+        _lib.check(_gemm("lr_int8_gemm_noalloc", a, b, rs, cs, bias, out), "lr_int8_gemm_noalloc")
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert _lib.device_status(clear=True) == 0
