@@ -31,7 +31,7 @@
 #define LR_GEMM_STAGES2 6
 #endif
 #ifndef LR_GEMM_L2_HINTS  // 0: default policy; 1: A panel evict-last; 2: also B evict-first
-#define LR_GEMM_L2_HINTS 0
+#define LR_GEMM_L2_HINTS 1
 #endif
 #ifndef LR_GEMM_STREAM_STORES  // 1: evict-first (st.global.cs) output stores
 #define LR_GEMM_STREAM_STORES 0
@@ -40,7 +40,7 @@
 #define LR_GEMM_TMA_OUT 1
 #endif
 #ifndef LR_GEMM_OUT_EVICT_FIRST  // L2 policy of those stores: 1 evict-first, 0 normal
-#define LR_GEMM_OUT_EVICT_FIRST 0
+#define LR_GEMM_OUT_EVICT_FIRST 1
 #endif
 
 namespace lr {
@@ -1209,10 +1209,18 @@ struct Destinations {
 };
 
 // M-blocks per raster group: as many as keep the group's A panel (rows x K
-// bytes) within a quarter-to-half of the 126 MB L2, so the weights stream
-// from HBM about once per group.
+// bytes) within LR_GEMM_PANEL_MB, so the weights stream from HBM about once
+// per group.
+// L2 budget of a raster group's A panel. With the A panel evict-last and the
+// output stores evict-first, 24 MB keeps the panel resident across the group's
+// N sweeps (FFN-up 12240x6144->24576: 1.14 GB of DRAM traffic per launch
+// against 1.60 GB at 48 MB with the default policies; a 64-80 MB panel, the
+// whole A matrix, thrashed: 2.4 GB).
+#ifndef LR_GEMM_PANEL_MB
+#define LR_GEMM_PANEL_MB 24
+#endif
 int raster_group(int block_rows, int num_m, int K) {
-  const int64_t budget = 48ll << 20;
+  const int64_t budget = (int64_t)LR_GEMM_PANEL_MB << 20;
   int64_t g = budget / ((int64_t)block_rows * (K > 0 ? K : 1));
   if (g < 1) g = 1;
   return (int)(g < num_m ? g : num_m);
