@@ -178,6 +178,44 @@ __device__ __forceinline__ int quant_i8(float v, float s, bool gpu) {
 #ifndef LR_QUANT_FAST_GPU
 #define LR_QUANT_FAST_GPU 1  // 0: div.full.f32 on every element in the gpu arithmetic (tuning knob)
 #endif
+__device__ __forceinline__ uint2 pack_q8(const uint32_t (&b)[8]) {
+  const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+  return make_uint2(lo, hi);
+}
+// The quotients themselves: RNE(v / s) in the chosen arithmetic.
+__device__ __forceinline__ uint2 quant8_exact(const uint4& v, float s, bool gpu) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float f[8];
+  unpack8(v, f);
+  uint32_t b[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(gpu ? div_full(f[e], s) : __fdiv_rn(f[e], s), kMagic));
+  return pack_q8(b);
+}
+// The reciprocal form alone: the bytes of RNE(v * (1/s)), with `near_tie`
+// set if any of them lies within 2^-14 of a rounding tie (then the chunk must
+// be redone by quant8_exact). Lets a kernel branch once for several chunks.
+__device__ __forceinline__ uint2 quant8_fast(const uint4& v, float inv, bool& near_tie) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float f[8];
+  unpack8(v, f);
+  uint32_t b[8];
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 magic2 = make_float2(kMagic, kMagic);
+  const float2 nmagic2 = make_float2(-kMagic, -kMagic);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const float2 q0 = __fmul2_rn(make_float2(f[e], f[e + 1]), inv2);
+    const float2 t = __fadd2_rn(q0, magic2);
+    const float2 r = __fadd2_rn(t, nmagic2);
+    const float2 d = __fadd2_rn(q0, make_float2(-r.x, -r.y));
+    near_tie |= (fabsf(d.x) > 0.49993896484375f) | (fabsf(d.y) > 0.49993896484375f);  // 0.5 - 2^-14
+    b[e] = __float_as_uint(t.x);
+    b[e + 1] = __float_as_uint(t.y);
+  }
+  return pack_q8(b);
+}
 __device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool gpu) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   float f[8];
@@ -186,9 +224,7 @@ __device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool
   if (gpu && !LR_QUANT_FAST_GPU) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(div_full(f[e], s), kMagic));
-    const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
-    const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
-    return make_uint2(lo, hi);
+    return pack_q8(b);
   }
   bool near_tie = false;
   const float2 inv2 = make_float2(inv, inv);
@@ -208,9 +244,7 @@ __device__ __forceinline__ uint2 quant8(const uint4& v, float s, float inv, bool
 #pragma unroll
     for (int e = 0; e < 8; ++e) b[e] = __float_as_uint(__fadd_rn(gpu ? div_full(f[e], s) : __fdiv_rn(f[e], s), kMagic));
   }
-  const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
-  const uint32_t hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
-  return make_uint2(lo, hi);
+  return pack_q8(b);
 }
 
 // Read-only streaming loads (bypass L1 allocation for one-touch data).

@@ -80,7 +80,12 @@ __device__ __forceinline__ const bf16* table_row_ptr(const bf16* table, int64_t 
                                                      int64_t sequence, int64_t row, bool& bad) {
   bad = false;
   if (table == nullptr) return nullptr;
-  const int64_t tr = indices[row % sequence];
+  // row % sequence without the 64-bit division routine in the common cases
+  // (one batch: row < sequence; both below 2^31: a 32-bit remainder)
+  const int64_t pos = row < sequence ? row
+                      : ((row | sequence) >> 31) == 0 ? (int64_t)((uint32_t)row % (uint32_t)sequence)
+                                                      : row % sequence;
+  const int64_t tr = indices[pos];
   if (tr < 0 || tr >= table_rows) {
     bad = true;
     return nullptr;

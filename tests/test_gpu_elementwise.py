@@ -197,7 +197,8 @@ def test_residual_fusion_equals_separate_kernels():
 
 
 @pytest.mark.parametrize("b,s,d", [(1, 1, 8), (2, 7, 192), (1, 129, 6144), (3, 5, 5376), (1, 3, 100),
-                                   (1, 2, 24576)])
+                                   (1, 2, 24576), (2, 3, 2048), (1, 4, 3072), (2, 2, 4112), (1, 3, 7168),
+                                   (2, 3, 8192), (3, 4, 4096)])
 def test_rms_shapes_vs_oracle_tree(b, s, d):
     gen = torch.Generator().manual_seed(b * 7 + s * 13 + d)
     x = torch.randn(b, s, d, generator=gen).to(torch.bfloat16)
