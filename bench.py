@@ -53,6 +53,9 @@ def parse_args():
                    help="block workload at N > 1: 'peer' writes the FFN-down GEMM's output rows straight into every "
                         "rank's gathered tensor over NVLink (the epilogue is the all-gather); 'nccl' runs "
                         "all_gather_into_tensor after the block")
+    p.add_argument("--eager", action="store_true",
+                   help="block workload: time the steps as eager launches instead of one CUDA-graph replay of the "
+                        "K steps (every launch and the gather barrier of each step captured)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--workload", choices=["block", "stack", "sweep", "flash", "reference_kernels", "kernel"],
@@ -387,18 +390,61 @@ def run_ours(args, rank, world, local):
         step(x, out=out_buf)
     torch.cuda.synchronize()
 
+    ev = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))  # noqa: E731
+    # events inside a captured graph are record nodes of their own (external)
+    ev_x = lambda: (torch.cuda.Event(enable_timing=True, external=True),  # noqa: E731
+                    torch.cuda.Event(enable_timing=True, external=True))
+    graph, graph_note = None, None
+    if not args.eager:
+        # The K timed steps as one CUDA graph: the same launches (and, at N > 1,
+        # the same stream-ordered NCCL barrier per step) replayed without the
+        # host issuing them one by one. Every rank agrees on the outcome of the
+        # capture before any rank replays; a failed capture times eager launches.
+        ffn = [ev_x() for _ in range(args.steps)]
+        ag = [ev_x() for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        err = None
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(args.steps):
+                    out = step(x, ffn[i], ag[i], out_buf)
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            graph, err = None, f"{type(exc).__name__}: {exc}"[:200]
+        torch.cuda.synchronize()
+        if world > 1:
+            okg = torch.tensor([0 if graph is None else 1], device=dev)
+            dist.all_reduce(okg, op=dist.ReduceOp.MIN)
+            if okg.item() == 0:
+                graph = None
+                err = err or "capture failed on another rank"
+        if graph is not None:
+            graph.replay()  # one untimed replay
+            torch.cuda.synchronize()
+            graph_note = {"timed": "one CUDA-graph replay of the K steps",
+                          "launches_per_step": block.LAUNCHES_PER_FORWARD}
+        else:
+            graph_note = {"timed": "eager launches", "capture_error": err}
+            ffn = [ev() for _ in range(args.steps)]
+            ag = [ev() for _ in range(args.steps)]
+    else:
+        graph_note = {"timed": "eager launches (--eager)"}
+        ffn = [ev() for _ in range(args.steps)]
+        ag = [ev() for _ in range(args.steps)]
+
     sampler = clock_sampler(dev, local) if rank == 0 else None
     if sampler:
         sampler.start()
-    ev = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))  # noqa: E731
-    ffn = [ev() for _ in range(args.steps)]
-    ag = [ev() for _ in range(args.steps)]
     start, end = ev()
     barrier()
     torch.cuda.synchronize()
     start.record()
-    for i in range(args.steps):
-        out = step(x, ffn[i], ag[i], out_buf)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.steps):
+            out = step(x, ffn[i], ag[i], out_buf)
     end.record()
     torch.cuda.synchronize()
     barrier()
@@ -494,6 +540,9 @@ def run_ours(args, rank, world, local):
     ceiling = None
     if rank == 0:
         ceiling = int8_ceiling_cublaslt(m, W.HIDDEN, W.FFN, dev)
+    # a graph holding NCCL calls is released before the process group goes
+    torch.cuda.synchronize()
+    graph = None
     if peer is not None:
         torch.cuda.synchronize()
         barrier()
@@ -565,6 +614,7 @@ def run_ours(args, rank, world, local):
         "clocks": clocks,
         "gpu_launches": block.LAUNCHES_PER_FORWARD * args.steps,
         "device_status": status,
+        "step_graph": graph_note,
         "e2e": e2e,
     }
     if world == 1 and not args.no_cpu_baseline:
